@@ -1,0 +1,133 @@
+/* attn_flash.h -- C ABI of the B200 (sm_100a) bf16 flash-attention forward.
+ *
+ * Drop-in for the attention entry points of flash.c (liujiang833/transfer_station):
+ * the same names, the same argument meaning, the same bk contract. What changes is where
+ * the tensors live: every tensor pointer here is a DEVICE pointer (cudaMalloc'd, or
+ * managed memory), and the caller-owned scratch block is device memory too.
+ *
+ * Tensor layouts (all contiguous, row-major, no strides -- as in flash.c):
+ *   Q  bf16 bit patterns (uint16_t)  [Hq ][Sq][D]
+ *   K  bf16 bit patterns             [Hkv][Sk][D]
+ *   V  bf16 bit patterns             [Hkv][Sk][D], or V^T [Hkv][D][Sk] when v_prepacked=1
+ *   O  fp32                          [Hq ][Sq][D]
+ * Query head h reads kv head h / (Hq/Hkv): MHA (Hkv==Hq), GQA, MQA (Hkv==1).
+ * Batch is folded into the head axis: Q [B*Hq][Sq][D], K/V [B*Hkv][Sk][D] maps batch b's
+ * head hq to kv head b*Hkv + hq/group, which is exactly (b*Hq+hq)/group.
+ * Scale is 1/sqrt(D). causal uses the bottom-right convention: query row i attends keys
+ * j <= Sk - Sq + i; a row that attends no key at all gets a zero output row.
+ *
+ * Nothing here allocates device memory. Every call is asynchronous on its stream except
+ * attn_flash(), which keeps the reference's blocking, void-returning contract.
+ */
+#ifndef ATTN_FLASH_B200_H
+#define ATTN_FLASH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* bk contract, unchanged from flash.c:132-134: a power of two in [16, 4096]; anything
+ * else prints the contract to stderr and abort()s, at both doors (attn_flash and
+ * attn_flash_scratch_bytes), exactly as flash.c:641-647 does. */
+#define ATTN_BK_MIN 16
+#define ATTN_BK_MAX 4096
+#define ATTN_BK_DEFAULT 128
+
+/* Scratch alignment. flash.c:607 used a 64-B cache line; device scratch wants 256 B
+ * (cudaMalloc returns 256-B aligned blocks, so any cudaMalloc'd block qualifies). */
+#define ATTN_SCRATCH_ALIGN 256
+
+/* The largest key tile the B200 kernel runs (keys per TMEM score tile). bk values above it
+ * are legal and run with this tile; bk values below 128 run with this tile too (the GPU
+ * result does not depend on bk beyond bf16 rounding noise, as on the CPU). */
+#define ATTN_GPU_KEY_TILE 128
+
+/* Largest head_dim the kernels accept. */
+#define ATTN_D_MAX 256
+
+/* Decode partial rows the scratch block holds (split-KV partials (m, l, acc[D])).
+ * Scratch size stays independent of Sq and Sk, as in flash.c; a call whose split-KV plan
+ * would need more partial rows uses fewer splits. */
+#define ATTN_PARTIAL_ROWS 32768
+
+/* Status codes of the *_stream entry points. */
+#define ATTN_OK 0
+#define ATTN_ERR_ARGS -1        /* bad shape / null pointer / Hq % Hkv != 0 / D out of range */
+#define ATTN_ERR_ALIGN -2       /* a device pointer is not 16-byte aligned */
+#define ATTN_ERR_CUDA -3        /* a CUDA runtime/driver call failed */
+#define ATTN_ERR_DEVICE -4      /* the kernel reported a bounded wait that ran out (see scratch status) */
+#define ATTN_ERR_NOT_SM100 -5   /* the current device is not compute capability 10.x */
+
+/* Per-phase timers of flash.c:704-706. On the GPU the four phases run fused in one kernel,
+ * so attn_flash() writes zeros into *tm when tm != NULL (packv is always 0: V is never
+ * transposed -- the tensor core reads it in place). Time the kernel with CUDA events. */
+struct attn_times {
+    double packv, qxk, softmax, sxv;
+};
+
+/* Bytes of device scratch one attn_flash call needs for this head_dim and key-block size.
+ * Replaces flash.c:679-682 (attn_flash_scratch_bytes). Validates bk (abort on violation,
+ * as flash.c). Independent of Sq and Sk: a status word plus ATTN_PARTIAL_ROWS split-KV
+ * partial rows of (D + 2) floats. */
+size_t attn_flash_scratch_bytes(int D, int bk);
+
+/* Tile-config picker. Replaces attn_flash_pick_bk(int D, size_t l2_bytes), specified at
+ * README.md:137-140,359-436 of the reference (absent from its shipped flash.c). First the
+ * reference's analytical model at the GPU's query block BQ=128: the largest power of two
+ * bk in [16, 4096] with 2*(6*bk*(D+BQ) + 6*BQ*D + 4*D + 12*BQ) <= l2_bytes (floor 16, cap
+ * 4096, D < 1 clamped to 1, size_t arithmetic throughout); then clamped to
+ * ATTN_GPU_KEY_TILE, the largest key tile the B200 kernel has. Always a legal bk. */
+int attn_flash_pick_bk(int D, size_t l2_bytes);
+
+/* The attention forward. Replaces flash.c:727-864 (static attn_flash). Device pointers.
+ * Blocking: returns after the result is in O, like the CPU reference. Aborts with a
+ * message on a bad bk (the reference contract) and on any other error (the void signature
+ * cannot report one; use attn_flash_stream for a status code). */
+void attn_flash(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O, int Hq,
+                int Hkv, int Sq, int Sk, int D, int causal, int bk, void *scratch,
+                int v_prepacked, struct attn_times *tm);
+
+/* Asynchronous variant of attn_flash on an explicit stream (a cudaStream_t passed as
+ * void*; NULL = legacy default stream). Same arguments and semantics as attn_flash;
+ * returns ATTN_OK or a negative status (bk is still validated by abort). A device-side
+ * failure (a bounded wait that ran out) is recorded in the scratch status word: read it
+ * with attn_flash_status. Concurrent calls must use distinct scratch blocks. */
+int attn_flash_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O,
+                      int Hq, int Hkv, int Sq, int Sk, int D, int causal, int bk,
+                      void *scratch, int v_prepacked, void *stream);
+
+/* Synchronises `stream`, reads and clears the device status word in `scratch`.
+ * Returns ATTN_OK, or ATTN_ERR_DEVICE when a kernel on that scratch reported a failure
+ * (the raw device code goes to *device_code when non-NULL), or ATTN_ERR_CUDA. */
+int attn_flash_status(void *scratch, void *stream, int *device_code);
+
+/* Human-readable name of a status code. */
+const char *attn_flash_strerror(int status);
+
+/* Key-sharded partial attention for multi-GPU long-context decode (no counterpart in
+ * flash.c, whose single call covers all keys; this is the per-GPU half of the key split
+ * of flash.c:798's key loop). K and V hold keys [k_begin, k_begin + Sk_local) of a key
+ * axis of length Sk_total; masking uses global key positions. Writes, per query row r of
+ * [Hq*Sq], the reference max m[r] in base-2 units of the scaled score (the partial's
+ * exponents are exp2(s*scale*log2(e) - m[r]); -inf if the row saw no key), the
+ * denominator l[r] and the UNnormalised accumulator acc[r][D]. */
+int attn_flash_partial_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V,
+                              float *m, float *l, float *acc, int Hq, int Hkv, int Sq,
+                              int Sk_local, int Sk_total, int k_begin, int D, int causal,
+                              int bk, void *scratch, int v_prepacked, void *stream);
+
+/* Merges nparts partials laid out [nparts][rows] (m, l) and [nparts][rows][D] (acc), as
+ * produced by attn_flash_partial_stream on disjoint key ranges, into O [rows][D] fp32:
+ * O = sum_s 2^(m_s - m*) acc_s / sum_s 2^(m_s - m*) l_s (a zero row where every l_s is 0),
+ * m* = max_s m_s. */
+int attn_flash_combine_stream(const float *m, const float *l, const float *acc, int nparts,
+                              int rows, int D, float *O, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ATTN_FLASH_B200_H */

@@ -1,0 +1,151 @@
+"""transfer_station_b200 -- B200 (sm_100a) bf16 flash-attention forward behind flash.c's C API.
+
+The product is the in-tree shared library ``lib/libattn_flash_b200.so`` (C host layer +
+tcgen05/TMA/TMEM CUDA kernels) whose entry points are declared in ``include/attn_flash.h``.
+This module is the thin Python mirror of that C ABI (ctypes), used by the tests and the
+benchmark: same names, same argument meaning, same error behaviour. It never computes
+anything itself -- if the library is missing it raises, there is no fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "lib" / "libattn_flash_b200.so"
+
+ATTN_BK_MIN = 16
+ATTN_BK_MAX = 4096
+ATTN_BK_DEFAULT = 128
+ATTN_SCRATCH_ALIGN = 256
+ATTN_GPU_KEY_TILE = 128
+ATTN_D_MAX = 256
+ATTN_PARTIAL_ROWS = 32768
+
+ATTN_OK = 0
+ATTN_ERR_ARGS = -1
+ATTN_ERR_ALIGN = -2
+ATTN_ERR_CUDA = -3
+ATTN_ERR_DEVICE = -4
+ATTN_ERR_NOT_SM100 = -5
+
+# Every symbol include/attn_flash.h declares, with its ctypes signature.
+_u16p = ctypes.c_void_p
+_f32p = ctypes.c_void_p
+EXPORTS = {
+    "attn_flash_scratch_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    "attn_flash_pick_bk": (ctypes.c_int, [ctypes.c_int, ctypes.c_size_t]),
+    "attn_flash": (None, [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 7 + [ctypes.c_void_p, ctypes.c_int,
+                                                                                 ctypes.c_void_p]),
+    "attn_flash_stream": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 7 + [ctypes.c_void_p,
+                                                                                          ctypes.c_int,
+                                                                                          ctypes.c_void_p]),
+    "attn_flash_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
+    "attn_flash_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "attn_flash_partial_stream": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 10 +
+                                  [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "attn_flash_combine_stream": (ctypes.c_int, [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                 _f32p, ctypes.c_void_p]),
+}
+
+_lib = None
+
+
+class AttnError(RuntimeError):
+    """A non-zero status from the C ABI."""
+
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        super().__init__(f"{what}: status {status} ({strerror(status)})" if what else strerror(status))
+
+
+def load_library(path: os.PathLike | str | None = None) -> ctypes.CDLL:
+    """Loads the in-tree library (raises FileNotFoundError when it has not been built)."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise FileNotFoundError(f"{p} is missing: run `python -m transfer_station_b200.build` (no CPU fallback)")
+    lib = ctypes.CDLL(str(p))
+    for name, (res, args) in EXPORTS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+def strerror(status: int) -> str:
+    return load_library().attn_flash_strerror(status).decode()
+
+
+def attn_flash_scratch_bytes(D: int, bk: int) -> int:
+    """flash.c:679-682. Aborts the process on an illegal bk, exactly like the reference."""
+    return int(load_library().attn_flash_scratch_bytes(D, bk))
+
+
+def attn_flash_pick_bk(D: int, l2_bytes: int) -> int:
+    return int(load_library().attn_flash_pick_bk(D, l2_bytes))
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else int(t.data_ptr())
+
+
+def _stream_handle(stream) -> int:
+    if stream is None:
+        import torch
+
+        return int(torch.cuda.current_stream().cuda_stream)
+    return int(getattr(stream, "cuda_stream", stream))
+
+
+def attn_flash_stream(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_prepacked=0, stream=None) -> int:
+    """Asynchronous attention on a torch stream (default: the current stream). Tensors are
+    CUDA torch tensors: Q/K/V int16 or uint16 bf16 bit patterns (or torch.bfloat16), O float32,
+    scratch a uint8 tensor of attn_flash_scratch_bytes(D, bk) bytes. Returns the status."""
+    return int(load_library().attn_flash_stream(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), Hq, Hkv, Sq, Sk, D,
+                                                 int(causal), bk, _ptr(scratch), int(v_prepacked),
+                                                 _stream_handle(stream)))
+
+
+def attn_flash(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_prepacked=0) -> None:
+    """The blocking, void entry (flash.c:727): runs on the legacy default stream, aborts the
+    process on error like the C function. Prefer attn_flash_checked in tests."""
+    load_library().attn_flash(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), Hq, Hkv, Sq, Sk, D, int(causal), bk,
+                              _ptr(scratch), int(v_prepacked), None)
+
+
+def attn_flash_status(scratch, stream=None) -> tuple[int, int]:
+    code = ctypes.c_int(0)
+    rc = load_library().attn_flash_status(_ptr(scratch), _stream_handle(stream), ctypes.byref(code))
+    return int(rc), int(code.value)
+
+
+def attn_flash_checked(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_prepacked=0, stream=None) -> None:
+    """attn_flash_stream + attn_flash_status, raising AttnError instead of aborting."""
+    rc = attn_flash_stream(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_prepacked, stream)
+    if rc != ATTN_OK:
+        raise AttnError(rc, "attn_flash_stream")
+    rc, code = attn_flash_status(scratch, stream)
+    if rc != ATTN_OK:
+        raise AttnError(rc, f"attn_flash_status (device code {code})")
+
+
+def attn_flash_partial_stream(Q, K, V, m, l, acc, Hq, Hkv, Sq, Sk_local, Sk_total, k_begin, D, causal, bk, scratch,
+                              v_prepacked=0, stream=None) -> int:
+    return int(load_library().attn_flash_partial_stream(_ptr(Q), _ptr(K), _ptr(V), _ptr(m), _ptr(l), _ptr(acc), Hq,
+                                                        Hkv, Sq, Sk_local, Sk_total, k_begin, D, int(causal), bk,
+                                                        _ptr(scratch), int(v_prepacked), _stream_handle(stream)))
+
+
+def attn_flash_combine_stream(m, l, acc, nparts, rows, D, O, stream=None) -> int:
+    return int(load_library().attn_flash_combine_stream(_ptr(m), _ptr(l), _ptr(acc), nparts, rows, D, _ptr(O),
+                                                        _stream_handle(stream)))
+
+
+__all__ = [n for n in dir() if n.startswith("attn_") or n.startswith("ATTN_")] + [
+    "AttnError", "load_library", "strerror", "LIB_PATH", "EXPORTS"]

@@ -1,0 +1,230 @@
+/* attn_flash.c -- the C host layer of the B200 attention path.
+ *
+ * Mirrors the driver half of flash.c's attn_flash (flash.c:727-772: bk check, group,
+ * scale, scratch carve) and its two sizing entry points, then hands a validated problem to
+ * the CUDA launchers. No allocation happens here: the only device memory touched besides
+ * the caller's tensors is the caller-owned scratch block.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "attn_flash.h"
+#include "fa_launch.h"
+
+/* flash.c:641-647: a bk the caller did not also size scratch with must fail loudly, never
+ * mis-stride a tile. Same bounds, same message shape, same abort(). */
+static void attn_bk_check(int bk, const char *who) {
+    if (bk < ATTN_BK_MIN || bk > ATTN_BK_MAX || (bk & (bk - 1)) != 0) {
+        fprintf(stderr, "%s: bk=%d is invalid -- bk must be a POWER OF TWO in [%d, %d]\n", who, bk, ATTN_BK_MIN,
+                ATTN_BK_MAX);
+        abort();
+    }
+}
+
+/* Scratch carve: status word, then partial m, l, acc sized for ATTN_PARTIAL_ROWS rows at
+ * this head_dim. One function measures and carves, as flash.c:658-672 insists. */
+typedef struct ts_scratch {
+    int *status;
+    float *m, *l, *acc;
+} ts_scratch;
+
+static size_t ts_scratch_layout(void *base, int D, ts_scratch *s) {
+    const size_t a = ATTN_SCRATCH_ALIGN;
+    const size_t d = D < 1 ? 1u : (size_t)D;
+    const size_t rows = ATTN_PARTIAL_ROWS;
+    size_t off = 0;
+    char *b = (char *)base;
+    if (s) s->status = base ? (int *)(b + off) : NULL;
+    off += TS_SCRATCH_CTRL_BYTES;
+    off = (off + a - 1) & ~(a - 1);
+    if (s) s->m = base ? (float *)(b + off) : NULL;
+    off += rows * sizeof(float);
+    off = (off + a - 1) & ~(a - 1);
+    if (s) s->l = base ? (float *)(b + off) : NULL;
+    off += rows * sizeof(float);
+    off = (off + a - 1) & ~(a - 1);
+    if (s) s->acc = base ? (float *)(b + off) : NULL;
+    off += rows * d * sizeof(float);
+    return (off + a - 1) & ~(a - 1);
+}
+
+size_t attn_flash_scratch_bytes(int D, int bk) {
+    attn_bk_check(bk, "attn_flash_scratch_bytes");
+    return ts_scratch_layout(NULL, D, NULL);
+}
+
+/* README.md:359-436 of the reference: working_set(D, bk) = 6*bk*(D+BQ) + 6*BQ*D + 4*D +
+ * 12*BQ, pick the largest power-of-two bk with 2*working_set <= l2_bytes; never below
+ * ATTN_BK_MIN (even if nothing fits), never above ATTN_BK_MAX; D < 1 clamped to 1; D
+ * widened to size_t before any arithmetic (the reference's own overflow fix). The GPU's
+ * query block is BQ = 128. The result is then capped at the kernel's key tile. */
+int attn_flash_pick_bk(int D, size_t l2_bytes) {
+    const size_t BQ = 128;
+    const size_t d = D < 1 ? 1u : (size_t)D;
+    const size_t per_bk = 6u * (d + BQ);
+    const size_t fixed = 6u * BQ * d + 4u * d + 12u * BQ;
+    const size_t half = l2_bytes / 2u; /* 2*ws <= l2  <=>  ws <= floor(l2/2) */
+    int best = ATTN_BK_MIN;
+    for (int bk = ATTN_BK_MIN; bk <= ATTN_BK_MAX; bk *= 2) {
+        const size_t ws = per_bk * (size_t)bk + fixed;
+        if (ws > half) break;
+        best = bk;
+    }
+    return best < ATTN_GPU_KEY_TILE ? best : ATTN_GPU_KEY_TILE;
+}
+
+const char *attn_flash_strerror(int status) {
+    switch (status) {
+    case ATTN_OK: return "ok";
+    case ATTN_ERR_ARGS: return "invalid arguments (shape, null pointer, Hq % Hkv, or D outside [1, 256])";
+    case ATTN_ERR_ALIGN: return "misaligned pointer";
+    case ATTN_ERR_CUDA: return "CUDA runtime/driver error";
+    case ATTN_ERR_DEVICE: return "device-side failure reported in the scratch status word (bounded wait ran out)";
+    case ATTN_ERR_NOT_SM100: return "current device is not a compute-capability 10.x (B200) GPU";
+    default: return "unknown status";
+    }
+}
+
+/* Split-KV plan: pick nsplit minimising the modelled makespan
+ *   T(s) = ceil(ctas*s / SMs) * (blocks/s + 1)
+ * (the +1 is the per-CTA prologue/epilogue, in key-block units), subject to the partial
+ * rows fitting the scratch and every split keeping >= 2 key blocks. */
+static void ts_plan_splits(fa_problem *p, int ctas) {
+    const long long rows = (long long)p->Hq * p->Sq;
+    const int nblk = (p->Sk + ATTN_GPU_KEY_TILE - 1) / ATTN_GPU_KEY_TILE;
+    const int sms = ts_num_sms();
+    long long cap = rows > 0 ? (long long)ATTN_PARTIAL_ROWS / rows : 0;
+    int smax = nblk / 2;
+    if (smax > cap) smax = (int)cap;
+    if (smax > 256) smax = 256;
+    int best = 1;
+    double best_t = 1e300;
+    for (int s = 1; s <= (smax > 1 ? smax : 1); ++s) {
+        const int bps = (nblk + s - 1) / s;
+        const int seff = (nblk + bps - 1) / bps;
+        if (seff != s) continue; /* same plan as a smaller s */
+        const long long tot = (long long)ctas * s;
+        const double waves = (double)((tot + sms - 1) / (sms > 0 ? sms : 1));
+        const double t = waves * ((double)bps + 1.0);
+        if (t < best_t * 0.999) {
+            best_t = t;
+            best = s;
+        }
+    }
+    const int bps = (nblk + best - 1) / best;
+    p->nsplit = best;
+    p->keys_per_split = bps * ATTN_GPU_KEY_TILE;
+}
+
+static int ts_validate(const void *Q, const void *K, const void *V, int Hq, int Hkv, int Sq, int Sk, int D,
+                       const void *scratch) {
+    if (!Q || !K || !V || !scratch) return ATTN_ERR_ARGS;
+    if (Hq < 1 || Hkv < 1 || Hq % Hkv != 0 || Sq < 1 || Sk < 1 || D < 1 || D > ATTN_D_MAX) return ATTN_ERR_ARGS;
+    if ((long long)Hq * Sq > 0x7fffffffLL || (long long)Hkv * Sk > 0x7fffffffLL) return ATTN_ERR_ARGS;
+    if (((uintptr_t)scratch) & 15u) return ATTN_ERR_ALIGN;
+    if (ts_cc_major() != 10) return ATTN_ERR_NOT_SM100;
+    return ATTN_OK;
+}
+
+static void ts_fill(fa_problem *p, const uint16_t *Q, const uint16_t *K, const uint16_t *V, int Hq, int Hkv,
+                    int Sq, int Sk, int D, int causal, int v_prepacked) {
+    memset(p, 0, sizeof *p);
+    p->Q = Q;
+    p->K = K;
+    p->V = V;
+    p->Hq = Hq;
+    p->Hkv = Hkv;
+    p->Sq = Sq;
+    p->Sk = Sk;
+    p->Sk_total = Sk;
+    p->k_begin = 0;
+    p->D = D;
+    p->causal = causal ? 1 : 0;
+    p->v_prepacked = v_prepacked ? 1 : 0;
+    p->scale_log2 = (1.0f / sqrtf((float)D)) * 1.4426950408889634f;
+    p->nsplit = 1;
+    p->keys_per_split = ((Sk + ATTN_GPU_KEY_TILE - 1) / ATTN_GPU_KEY_TILE) * ATTN_GPU_KEY_TILE;
+}
+
+static int ts_run(fa_problem *p, void *scratch, void *stream) {
+    ts_scratch s;
+    ts_scratch_layout(scratch, p->D, &s);
+    p->status = s.status;
+    const int ctas = ts_tc_supported(p) ? ts_tc_ctas_per_split(p) : (int)(((long long)p->Hq * p->Sq + 7) / 8);
+    ts_plan_splits(p, ctas);
+    if (p->nsplit > 1) {
+        p->part_m = s.m;
+        p->part_l = s.l;
+        p->part_acc = s.acc;
+    } else if (p->write_partials) {
+        p->part_m = p->out_m;
+        p->part_l = p->out_l;
+        p->part_acc = p->out_acc;
+    }
+    int rc = ts_clear_status(s.status, stream);
+    if (rc != ATTN_OK) return rc;
+    return ts_launch_attention(p, stream);
+}
+
+int attn_flash_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O, int Hq, int Hkv, int Sq,
+                      int Sk, int D, int causal, int bk, void *scratch, int v_prepacked, void *stream) {
+    attn_bk_check(bk, "attn_flash");
+    int rc = ts_validate(Q, K, V, Hq, Hkv, Sq, Sk, D, scratch);
+    if (rc != ATTN_OK) return rc;
+    if (!O) return ATTN_ERR_ARGS;
+    fa_problem p;
+    ts_fill(&p, Q, K, V, Hq, Hkv, Sq, Sk, D, causal, v_prepacked);
+    p.O = O;
+    return ts_run(&p, scratch, stream);
+}
+
+int attn_flash_partial_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *m, float *l,
+                              float *acc, int Hq, int Hkv, int Sq, int Sk_local, int Sk_total, int k_begin, int D,
+                              int causal, int bk, void *scratch, int v_prepacked, void *stream) {
+    attn_bk_check(bk, "attn_flash_partial");
+    int rc = ts_validate(Q, K, V, Hq, Hkv, Sq, Sk_local, D, scratch);
+    if (rc != ATTN_OK) return rc;
+    if (!m || !l || !acc || k_begin < 0 || Sk_total < (long long)k_begin + Sk_local) return ATTN_ERR_ARGS;
+    fa_problem p;
+    ts_fill(&p, Q, K, V, Hq, Hkv, Sq, Sk_local, D, causal, v_prepacked);
+    p.Sk_total = Sk_total;
+    p.k_begin = k_begin;
+    p.write_partials = 1;
+    p.out_m = m;
+    p.out_l = l;
+    p.out_acc = acc;
+    return ts_run(&p, scratch, stream);
+}
+
+int attn_flash_combine_stream(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
+                              float *O, void *stream) {
+    if (!m || !l || !acc || !O || nparts < 1 || rows < 0 || D < 1 || D > ATTN_D_MAX) return ATTN_ERR_ARGS;
+    if (ts_cc_major() != 10) return ATTN_ERR_NOT_SM100;
+    return ts_launch_combine(m, l, acc, nparts, rows, D, O, NULL, NULL, stream);
+}
+
+int attn_flash_status(void *scratch, void *stream, int *device_code) {
+    if (!scratch) return ATTN_ERR_ARGS;
+    ts_scratch s;
+    ts_scratch_layout(scratch, 1, &s);
+    int v = 0;
+    int rc = ts_read_status(s.status, stream, &v);
+    if (device_code) *device_code = v;
+    if (rc != ATTN_OK) return rc;
+    return v ? ATTN_ERR_DEVICE : ATTN_OK;
+}
+
+void attn_flash(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O, int Hq, int Hkv, int Sq, int Sk,
+                int D, int causal, int bk, void *scratch, int v_prepacked, struct attn_times *tm) {
+    int rc = attn_flash_stream(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_prepacked, NULL);
+    int code = 0;
+    if (rc == ATTN_OK) rc = attn_flash_status(scratch, NULL, &code);
+    if (tm) memset(tm, 0, sizeof *tm);
+    if (rc != ATTN_OK) {
+        fprintf(stderr, "attn_flash: %s (device code %d)\n", attn_flash_strerror(rc), code);
+        abort();
+    }
+}

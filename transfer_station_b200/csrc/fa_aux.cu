@@ -1,0 +1,228 @@
+// fa_aux.cu -- the CUDA-core side of the attention path:
+//   * fa_simt_kernel: the general-shape kernel (any head_dim 1..256, unaligned pointers,
+//     V^T with Sk not a multiple of 8). One warp per query row; same online-softmax state
+//     as flash.c:518-580 (bf16-rounded P, l summing the unrounded exponentials, zero row
+//     when no key is live), one key at a time.
+//   * fa_combine_kernel: merges split-KV partials (m, l, acc) into O, or into one partial.
+//   * status-word helpers and the top-level launcher called by the C host layer.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "attn_flash.h"
+#include "fa_launch.h"
+
+extern "C" int ts_launch_tc(const fa_problem *P, void *stream, int partial);
+
+namespace ts {
+
+__device__ __forceinline__ float ex2f(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
+
+struct SimtParams {
+    const uint16_t *Q, *K, *V;
+    float *O, *part_m, *part_l, *part_acc;
+    int Hq, Hkv, Sq, Sk, Sk_total, k_begin, D, causal, v_prepacked;
+    int keys_per_split, partial;
+    float scale_log2;
+};
+
+constexpr int kSimtMaxU = ATTN_D_MAX / 32;  // columns per lane
+
+__global__ void __launch_bounds__(256) fa_simt_kernel(const SimtParams p) {
+    const int lane = threadIdx.x & 31;
+    const long long total_rows = (long long)p.Hq * p.Sq;
+    const long long grow = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (grow >= total_rows) return;
+    const int split = blockIdx.y;
+    const int h = (int)(grow / p.Sq), i = (int)(grow % p.Sq);
+    const int kv = h / (p.Hq / p.Hkv);
+    const int kb0 = split * p.keys_per_split;
+    const int kb1 = min(p.Sk, kb0 + p.keys_per_split);
+    long long lim = p.causal ? ((long long)p.Sk_total - p.Sq + i - p.k_begin) : (long long)(p.Sk - 1);
+    const int kend = (int)max((long long)kb0, min((long long)kb1, lim + 1));
+
+    float q[kSimtMaxU], acc[kSimtMaxU];
+#pragma unroll
+    for (int u = 0; u < kSimtMaxU; ++u) {
+        const int c = lane + 32 * u;
+        q[u] = (c < p.D) ? bf16_bits_to_f32(p.Q[grow * p.D + c]) : 0.f;
+        acc[u] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    const uint16_t *Kh = p.K + (size_t)kv * p.Sk * p.D;
+    const uint16_t *Vh = p.V + (size_t)kv * p.Sk * p.D;
+    for (int k = kb0; k < kend; ++k) {
+        float part = 0.f;
+#pragma unroll
+        for (int u = 0; u < kSimtMaxU; ++u) {
+            const int c = lane + 32 * u;
+            if (c < p.D) part = fmaf(q[u], bf16_bits_to_f32(Kh[(size_t)k * p.D + c]), part);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        const float s = part * p.scale_log2;
+        if (s > m) {
+            const float alpha = (m == -INFINITY) ? 0.f : ex2f(m - s);
+            l *= alpha;
+#pragma unroll
+            for (int u = 0; u < kSimtMaxU; ++u) acc[u] *= alpha;
+            m = s;
+        }
+        const float e = ex2f(s - m);
+        l += e;
+        const float pb = __bfloat162float(__float2bfloat16_rn(e));
+#pragma unroll
+        for (int u = 0; u < kSimtMaxU; ++u) {
+            const int c = lane + 32 * u;
+            if (c < p.D) {
+                const float v = p.v_prepacked ? bf16_bits_to_f32(Vh[(size_t)c * p.Sk + k])
+                                              : bf16_bits_to_f32(Vh[(size_t)k * p.D + c]);
+                acc[u] = fmaf(pb, v, acc[u]);
+            }
+        }
+    }
+    if (p.partial) {
+        const size_t pr = (size_t)split * total_rows + grow;
+        if (lane == 0) {
+            p.part_m[pr] = m;
+            p.part_l[pr] = l;
+        }
+#pragma unroll
+        for (int u = 0; u < kSimtMaxU; ++u) {
+            const int c = lane + 32 * u;
+            if (c < p.D) p.part_acc[pr * p.D + c] = acc[u];
+        }
+    } else {
+        const float inv = (l > 0.f) ? 1.f / l : 0.f;
+#pragma unroll
+        for (int u = 0; u < kSimtMaxU; ++u) {
+            const int c = lane + 32 * u;
+            if (c < p.D) p.O[grow * p.D + c] = acc[u] * inv;
+        }
+    }
+}
+
+// One warp per row: O[r] = sum_s 2^(m_s - m*) acc_s[r] / sum_s 2^(m_s - m*) l_s[r].
+// With out_m != nullptr the merged partial (m*, L, unnormalised acc) is written instead.
+__global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict__ m, const float *__restrict__ l,
+                                                         const float *__restrict__ acc, int nparts, int rows, int D,
+                                                         float *__restrict__ out, float *__restrict__ out_m,
+                                                         float *__restrict__ out_l) {
+    const int lane = threadIdx.x & 31;
+    const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    float mx = -INFINITY;
+    for (int s = 0; s < nparts; ++s) mx = fmaxf(mx, m[(size_t)s * rows + r]);
+    float L = 0.f;
+    for (int s = 0; s < nparts; ++s) {
+        const float ms = m[(size_t)s * rows + r];
+        if (ms != -INFINITY) L = fmaf(ex2f(ms - mx), l[(size_t)s * rows + r], L);
+    }
+    const float inv = out_m ? 1.f : ((L > 0.f) ? 1.f / L : 0.f);
+    for (int c = lane; c < D; c += 32) {
+        float a = 0.f;
+        for (int s = 0; s < nparts; ++s) {
+            const float ms = m[(size_t)s * rows + r];
+            if (ms != -INFINITY) a = fmaf(ex2f(ms - mx), acc[((size_t)s * rows + r) * D + c], a);
+        }
+        out[(size_t)r * D + c] = a * inv;
+    }
+    if (out_m && lane == 0) {
+        out_m[r] = mx;
+        out_l[r] = L;
+    }
+}
+
+}  // namespace ts
+
+extern "C" int ts_num_sms(void) {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (dev < 64 && cached[dev]) return cached[dev];
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    if (dev < 64) cached[dev] = n;
+    return n;
+}
+
+extern "C" int ts_cc_major(void) {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    if (dev < 64 && cached[dev]) return cached[dev];
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return -1;
+    if (dev < 64) cached[dev] = v;
+    return v;
+}
+
+extern "C" int ts_launch_combine(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
+                                 float *O, float *out_m, float *out_l, void *stream) {
+    if (rows <= 0) return ATTN_OK;
+    const int warps = 8;
+    dim3 grid((rows + warps - 1) / warps);
+    ts::fa_combine_kernel<<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows, D, O,
+                                                                                      out_m, out_l);
+    return cudaGetLastError() == cudaSuccess ? ATTN_OK : ATTN_ERR_CUDA;
+}
+
+static int launch_simt(const fa_problem *P, void *stream, int partial) {
+    ts::SimtParams s;
+    s.Q = P->Q;
+    s.K = P->K;
+    s.V = P->V;
+    s.O = P->O;
+    s.part_m = P->part_m;
+    s.part_l = P->part_l;
+    s.part_acc = P->part_acc;
+    s.Hq = P->Hq;
+    s.Hkv = P->Hkv;
+    s.Sq = P->Sq;
+    s.Sk = P->Sk;
+    s.Sk_total = P->Sk_total;
+    s.k_begin = P->k_begin;
+    s.D = P->D;
+    s.causal = P->causal;
+    s.v_prepacked = P->v_prepacked;
+    s.keys_per_split = P->keys_per_split;
+    s.partial = partial;
+    s.scale_log2 = P->scale_log2;
+    const long long rows = (long long)P->Hq * P->Sq;
+    const int warps = 8;
+    dim3 grid((unsigned)((rows + warps - 1) / warps), P->nsplit);
+    ts::fa_simt_kernel<<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(s);
+    return cudaGetLastError() == cudaSuccess ? ATTN_OK : ATTN_ERR_CUDA;
+}
+
+extern "C" int ts_launch_attention(const fa_problem *P, void *stream) {
+    const int partial = (P->nsplit > 1 || P->write_partials) ? 1 : 0;
+    int rc = ts_tc_supported(P) ? ts_launch_tc(P, stream, partial) : launch_simt(P, stream, partial);
+    if (rc != ATTN_OK || P->nsplit <= 1) return rc;
+    const int rows = P->Hq * P->Sq;
+    return ts_launch_combine(P->part_m, P->part_l, P->part_acc, P->nsplit, rows, P->D,
+                             P->write_partials ? P->out_acc : P->O, P->write_partials ? P->out_m : nullptr,
+                             P->write_partials ? P->out_l : nullptr, stream);
+}
+
+extern "C" int ts_clear_status(int *status, void *stream) {
+    return cudaMemsetAsync(status, 0, sizeof(int), static_cast<cudaStream_t>(stream)) == cudaSuccess ? ATTN_OK
+                                                                                                    : ATTN_ERR_CUDA;
+}
+
+extern "C" int ts_read_status(int *status, void *stream, int *value) {
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (cudaStreamSynchronize(st) != cudaSuccess) return ATTN_ERR_CUDA;
+    int v = 0;
+    if (cudaMemcpy(&v, status, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return ATTN_ERR_CUDA;
+    if (v != 0 && cudaMemset(status, 0, sizeof(int)) != cudaSuccess) return ATTN_ERR_CUDA;
+    if (value) *value = v;
+    return ATTN_OK;
+}

@@ -1,0 +1,560 @@
+// fa_fwd_sm100.cu -- bf16 flash-attention forward on the Blackwell tensor core (sm_100a).
+//
+// Replaces the hot loop of flash.c's attn_flash (flash.c:779-861): qk_tile (flash.c:352-423)
+// becomes a tcgen05 MMA S = Q K^T with S in TMEM; softmax_block (flash.c:518-580) runs on
+// the TMEM score tile in softmax warpgroups (one thread per query row); pv_acc
+// (flash.c:433-510) becomes a second tcgen05 MMA O += P V whose A operand P is written back
+// into TMEM as bf16 and whose B operand V is read from shared memory in place -- MN-major
+// for V [keys][D], K-major for a pre-transposed V^T [D][Sk] -- so pack_vt (flash.c:327-342)
+// disappears. The final normalise (flash.c:851-860) is the epilogue.
+//
+// Work decomposition. The `group` query heads that share kv head `kv` are contiguous in Q
+// ([Hq][Sq][D] == [Hkv][group*Sq][D]), so each kv head owns one packed [group*Sq][D]
+// matrix of query rows that all read the same K/V. A CTA takes NQT tiles of 128 packed
+// rows (256 rows for NQT=2) and streams the kv head's K/V tiles once for all of them.
+// grid = (row tiles per kv head, Hkv, key splits).
+//
+// Roles (one CTA per SM): warp 0 issues TMA loads (Q once, then K_j, V_j alternating
+// through an NS-slot ring); warp 1 owns TMEM and issues the MMAs from one thread;
+// warps 4.. are softmax warpgroups, one per query tile, thread r of a warpgroup owning
+// TMEM lane r = query row r. Per key block j and tile t:
+//   MMA:      S_t = Q_t K_j^T                      -> commit s_full[t]
+//   softmax:  mask, row max, P = 2^(S*c - m) bf16 -> TMEM (aliasing S_t), l update,
+//             rescale O_t when its max moved       -> arrive p_full[t]
+//   MMA:      O_t += P_t V_j ; S_t = Q_t K_{j+1}^T  -> commit s_full[t]
+// tcgen05.commit fires only when every earlier MMA of the issuing thread finished, so the
+// s_full completion that delivers S_t(j) also proves PV_t(j-1) wrote O_t: the softmax can
+// rescale O_t right after reading S_t(j). With two tiles the tensor core computes one
+// tile's PV+QK while the other tile's softmax runs.
+//
+// Online-softmax state per row follows flash.c:535-576: running max m, alpha =
+// exp(m_old - m_new) (0 on a row's first live block), P rounded to bf16 while l sums the
+// UNrounded fp32 exponentials, a block with no live key leaves the state unchanged, and a
+// row that never sees a key ends with l == 0 and a zero output row. One refinement: the
+// running max is only moved when the block max exceeds it by more than 2^kRescaleLog2
+// (in exp2 units); otherwise the old max stays the reference and P may exceed 1 by at most
+// that factor. The quotient acc/l is the same mathematical value; this skips most O
+// rescales (TMEM round trips).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "attn_flash.h"
+#include "fa_launch.h"
+#include "sm100_ptx.cuh"
+
+namespace ts {
+
+constexpr int kBM = 128;              // query rows per tile (TMEM lanes)
+constexpr int kBN = ATTN_GPU_KEY_TILE;  // keys per tile
+constexpr float kRescaleLog2 = 8.0f;  // lazy max update threshold, in log2 units
+constexpr int kSmemBudget = 200 * 1024;
+
+struct TcParams {
+    float *O;
+    float *part_m, *part_l, *part_acc;
+    int *status;
+    int rows_per_kv;  // group * Sq
+    int total_rows;   // Hq * Sq
+    int Sq, Sk, Sk_total, k_begin;
+    int D, causal;
+    int keys_per_split;
+    float scale_log2;
+};
+
+template <int DP, int NQT>
+struct TcConfig {
+    static constexpr int QTILE = kBM * DP * 2;   // bytes of one Q tile
+    static constexpr int KVTILE = kBN * DP * 2;  // bytes of one K or V tile
+    static constexpr int NS_RAW = (kSmemBudget - NQT * QTILE) / KVTILE;
+    static constexpr int NS = NS_RAW > 8 ? 8 : NS_RAW;  // K/V ring slots
+    static constexpr int NBAR = 2 + 2 * NS + 2 * NQT;   // q_full, done, kv_full/empty, s/p_full
+    static constexpr int SMEM = 1024 + NQT * QTILE + NS * KVTILE + NBAR * 8 + 16;
+    static constexpr int THREADS = 128 + 128 * NQT;
+    static constexpr uint32_t TMEM_COLS = (NQT * kBN + NQT * DP) <= 256 ? 256u : 512u;
+    static_assert(NS >= 2, "K/V ring needs at least two slots");
+    static_assert(DP % 64 == 0 && DP <= 128, "padded head_dim must be 64 or 128");
+    static_assert(NQT * kBN + NQT * DP <= 512, "TMEM budget");
+};
+
+__device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+__device__ __forceinline__ uint32_t f2u(float f) { return __float_as_uint(f); }
+
+// Waits without honouring the abort flag: used only at teardown, to let TMA copies and MMAs
+// that are already in flight land before the CTA releases its shared memory and TMEM.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int *status) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            if (status) atomicOr(status, kDevErrTimeoutDrain);
+            return;
+        }
+    }
+}
+
+template <int DP, int NQT, bool VT, bool PARTIAL>
+__global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
+    fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                 const __grid_constant__ CUtensorMap tmV, const TcParams p) {
+    using C = TcConfig<DP, NQT>;
+    constexpr int NS = C::NS;
+    constexpr int NBOX_D = DP / 64;     // 64-element (128-byte) boxes across the head dim
+    constexpr int BOX_ROWS128 = 128 * 128;  // bytes of one [128 rows][64 cols] bf16 box
+
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_u32 = smem_u32(smem_raw);
+    const uint32_t base_u32 = (raw_u32 + 1023u) & ~1023u;
+    uint8_t *smem = smem_raw + (base_u32 - raw_u32);
+
+    const uint32_t sQ = base_u32;
+    const uint32_t sKV = base_u32 + NQT * C::QTILE;
+    const uint32_t bar0 = sKV + NS * C::KVTILE;
+    const uint32_t q_full = bar0;
+    const uint32_t done_bar = bar0 + 8;
+    auto kv_full = [&](int s) { return bar0 + 16 + 8u * s; };
+    auto kv_empty = [&](int s) { return bar0 + 16 + 8u * (NS + s); };
+    auto s_full = [&](int t) { return bar0 + 16 + 8u * (2 * NS + t); };
+    auto p_full = [&](int t) { return bar0 + 16 + 8u * (2 * NS + NQT + t); };
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + (bar0 - base_u32) + C::NBAR * 8);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    // ---------------- work item
+    const int kv = blockIdx.y;
+    const int split = blockIdx.z;
+    const int tile_idx = p.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
+    const int row0 = tile_idx * kBM * NQT;
+    const int kb0 = split * p.keys_per_split;            // local key range [kb0, kb1)
+    const int kb1 = min(p.Sk, kb0 + p.keys_per_split);
+    int kend = kb1;
+    if (p.causal) {
+        const int rlast = min(row0 + kBM * NQT, p.rows_per_kv) - 1;
+        const int i_hi = (row0 / p.Sq == rlast / p.Sq) ? (rlast % p.Sq) : (p.Sq - 1);
+        const long long lim = (long long)p.Sk_total - p.Sq + i_hi - p.k_begin;  // last live local key
+        if (lim + 1 < (long long)kend) kend = (int)max(lim + 1, (long long)kb0);
+    }
+    const int nblk = kend > kb0 ? (kend - kb0 + kBN - 1) / kBN : 0;
+
+    // ---------------- setup
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        mbar_init(done_bar, 1);
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(kv_full(s), 1);
+            mbar_init(kv_empty(s), 1);
+        }
+        for (int t = 0; t < NQT; ++t) {
+            mbar_init(s_full(t), 1);
+            mbar_init(p_full(t), 128);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ============================ TMA producer
+        if (lane == 0 && nblk > 0) {
+            int issued = 0;
+            bool ok = true;
+            mbar_expect_tx(q_full, NQT * C::QTILE);
+#pragma unroll
+            for (int t = 0; t < NQT; ++t)
+#pragma unroll
+                for (int b = 0; b < NBOX_D; ++b)
+                    tma_load_3d(sQ + t * C::QTILE + b * BOX_ROWS128, &tmQ, q_full, b * 64,
+                                row0 + t * kBM, kv);
+            const int nload = 2 * nblk;
+            for (int i = 0; i < nload; ++i) {
+                const int slot = i % NS;
+                const int round = i / NS;
+                if (round > 0 &&
+                    !mbar_wait(kv_empty(slot), (round - 1) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                    ok = false;
+                    break;
+                }
+                const int key0 = kb0 + (i >> 1) * kBN;
+                const uint32_t dst = sKV + slot * C::KVTILE;
+                const uint32_t bar = kv_full(slot);
+                mbar_expect_tx(bar, C::KVTILE);
+                if ((i & 1) == 0) {
+#pragma unroll
+                    for (int b = 0; b < NBOX_D; ++b)
+                        tma_load_3d(dst + b * (kBN * 128), &tmK, bar, b * 64, key0, kv);
+                } else if (!VT) {
+#pragma unroll
+                    for (int b = 0; b < NBOX_D; ++b)
+                        tma_load_3d(dst + b * (kBN * 128), &tmV, bar, b * 64, key0, kv);
+                } else {
+#pragma unroll
+                    for (int b = 0; b < kBN / 64; ++b)
+                        tma_load_3d(dst + b * (DP * 128), &tmV, bar, key0 + b * 64, 0, kv);
+                }
+                issued = i + 1;
+            }
+            if (!ok) {  // let the copies already in flight land before the CTA exits
+                drain_wait(q_full, 0, p.status);
+                for (int i = max(0, issued - NS); i < issued; ++i) drain_wait(kv_full(i % NS), (i / NS) & 1, p.status);
+            }
+        }
+    } else if (warp == 1) {
+        // ============================ MMA issuer (one thread)
+        if (lane == 0 && nblk > 0) {
+            constexpr uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, 0, 0);
+            constexpr uint32_t idesc_pv = idesc_bf16_f32(kBM, DP, 0, VT ? 0 : 1);
+            auto issue_qk = [&](int t, int slot) {
+                const uint32_t qa = sQ + t * C::QTILE;
+                const uint32_t kb = sKV + slot * C::KVTILE;
+                const uint32_t d_tmem = tmem_base + t * kBN;
+#pragma unroll
+                for (int ks = 0; ks < DP / 16; ++ks) {
+                    const uint32_t off = (ks >> 2) * BOX_ROWS128 + (ks & 3) * 32;
+                    umma_ss(d_tmem, sdesc_sw128(qa + off, 16, 1024), sdesc_sw128(kb + off, 16, 1024), idesc_qk,
+                            ks > 0 ? 1u : 0u);
+                }
+            };
+            auto issue_pv = [&](int t, int slot, bool accumulate) {
+                const uint32_t vb = sKV + slot * C::KVTILE;
+                const uint32_t d_tmem = tmem_base + NQT * kBN + t * DP;
+                const uint32_t a_tmem = tmem_base + t * kBN;
+#pragma unroll
+                for (int ks = 0; ks < kBN / 16; ++ks) {
+                    uint64_t bdesc;
+                    if (!VT)  // V [keys][D]: MN-major; LBO = next 64-column block of D, SBO = next 8 keys
+                        bdesc = sdesc_sw128(vb + ks * 16 * 128, kBN * 128, 1024);
+                    else      // V^T [D][keys]: K-major, like K
+                        bdesc = sdesc_sw128(vb + (ks >> 2) * (DP * 128) + (ks & 3) * 32, 16, 1024);
+                    umma_ts(d_tmem, a_tmem + ks * 8, bdesc, idesc_pv, (accumulate || ks > 0) ? 1u : 0u);
+                }
+            };
+            bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kDevErrTimeoutQ) &&
+                      mbar_wait(kv_full(0), 0, abort_flag, p.status, kDevErrTimeoutKV);
+            if (ok) {
+                tc_fence_after();
+#pragma unroll
+                for (int t = 0; t < NQT; ++t) {
+                    issue_qk(t, 0);
+                    tc_commit(s_full(t));
+                }
+                tc_commit(kv_empty(0));
+            }
+            for (int j = 0; ok && j < nblk; ++j) {
+                const int iV = 2 * j + 1, iK = 2 * j + 2;
+                const int sV = iV % NS, sK = iK % NS;
+                const bool more = j + 1 < nblk;
+#pragma unroll
+                for (int t = 0; t < NQT; ++t) {
+                    if (!mbar_wait(p_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutP)) { ok = false; break; }
+                    if (t == 0 && !mbar_wait(kv_full(sV), (iV / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    issue_pv(t, sV, j > 0);
+                    if (more) {
+                        if (t == 0) {
+                            if (!mbar_wait(kv_full(sK), (iK / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                        }
+                        issue_qk(t, sK);
+                    }
+                    tc_commit(s_full(t));
+                }
+                if (!ok) break;
+                tc_commit(kv_empty(sV));
+                if (more) tc_commit(kv_empty(sK));
+            }
+            // Every MMA issued above must finish before TMEM is released.
+            tc_commit(done_bar);
+            drain_wait(done_bar, 0, p.status);
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        // ============================ softmax / correction / epilogue
+        const int t = (warp - 4) >> 2;
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const int prow = row0 + t * kBM + r;  // packed row within this kv head
+        const bool valid = prow < p.rows_per_kv;
+        const int ipos = valid ? prow % p.Sq : 0;
+        const long long lim = p.causal ? ((long long)p.Sk_total - p.Sq + ipos - p.k_begin)
+                                       : (long long)(p.Sk - 1);  // last live local key of this row
+        const long long lastkey = min(lim, (long long)kb1 - 1);
+        const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        const uint32_t tS = tmem_base + lane_off + t * kBN;
+        const uint32_t tO = tmem_base + lane_off + NQT * kBN + t * DP;
+        const float sl2 = p.scale_log2;
+
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nblk; ++j) {
+            ok = mbar_wait(s_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutS);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
+            uint32_t sa[32], sb[32], sc[32], sd[32];
+            tmem_ld32x2(tS, tS + 32, sa, sb);
+            tmem_ld32x2(tS + 64, tS + 96, sc, sd);
+            float f[128];
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                f[c] = u2f(sa[c]);
+                f[32 + c] = u2f(sb[c]);
+                f[64 + c] = u2f(sc[c]);
+                f[96 + c] = u2f(sd[c]);
+            }
+            const long long key0 = kb0 + (long long)j * kBN;
+            const long long nv = lastkey - key0 + 1;
+            if (nv < kBN) {
+                const int nvalid = nv < 0 ? 0 : (int)nv;
+#pragma unroll
+                for (int c = 0; c < 128; ++c)
+                    if (c >= nvalid) f[c] = -INFINITY;
+            }
+            float mx0 = f[0], mx1 = f[1], mx2 = f[2], mx3 = f[3];
+#pragma unroll
+            for (int c = 4; c < 128; c += 4) {
+                mx0 = fmaxf(mx0, f[c]);
+                mx1 = fmaxf(mx1, f[c + 1]);
+                mx2 = fmaxf(mx2, f[c + 2]);
+                mx3 = fmaxf(mx3, f[c + 3]);
+            }
+            const float mb = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+            float m_new = m;
+            if (mb > m && (m == -INFINITY || (mb - m) * sl2 > kRescaleLog2)) m_new = mb;
+            const float alpha = (m_new == m) ? 1.f : ((m == -INFINITY) ? 0.f : ex2((m - m_new) * sl2));
+            const float ms = (m_new == -INFINITY) ? 0.f : __fmul_rn(m_new, sl2);
+            float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    // Rounded multiply, then subtract (never fused): the row's max element
+                    // gives exactly 2^0 = 1, as exp(S - m) does in flash.c:566.
+                    const float p0 = ex2(__fsub_rn(__fmul_rn(f[32 * cc + 2 * u], sl2), ms));
+                    const float p1 = ex2(__fsub_rn(__fmul_rn(f[32 * cc + 2 * u + 1], sl2), ms));
+                    rs0 += p0;
+                    rs1 += p1;
+                    pk[u] = pack_bf16x2(p0, p1);
+                }
+                tmem_st16(tS + cc * 16, pk);
+            }
+            l = l * alpha + (rs0 + rs1);
+            m = m_new;
+            // O_t holds P V through block j-1 (complete: S_t(j) was committed after it).
+            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                for (int cc = 0; cc < DP / 32; ++cc) {
+                    uint32_t o[32];
+                    tmem_ld32(tO + cc * 32, o);
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) o[u] = f2u(u2f(o[u]) * alpha);
+                    tmem_st32(tO + cc * 32, o);
+                }
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(p_full(t));
+        }
+        bool have_o = false;
+        if (ok && nblk > 0) {
+            have_o = mbar_wait(s_full(t), nblk & 1, abort_flag, p.status, kDevErrTimeoutS);
+            have_o = __all_sync(0xffffffffu, have_o);
+            ok = have_o;
+            if (have_o) tc_fence_after();
+        }
+        if (ok) {
+            // ------------------------ epilogue
+            const int D = p.D;
+            const size_t grow = (size_t)kv * p.rows_per_kv + prow;  // row of [Hq*Sq]
+            float *dst;
+            float mult;
+            if (PARTIAL) {
+                const size_t prow_g = (size_t)split * p.total_rows + grow;
+                if (valid) {
+                    p.part_m[prow_g] = (m == -INFINITY) ? -INFINITY : __fmul_rn(m, sl2);
+                    p.part_l[prow_g] = l;
+                }
+                dst = p.part_acc + prow_g * D;
+                mult = 1.f;
+            } else {
+                dst = p.O + grow * D;
+                mult = (l > 0.f) ? 1.f / l : 0.f;
+            }
+#pragma unroll
+            for (int cc = 0; cc < DP / 32; ++cc) {
+                uint32_t o[32];
+                if (have_o) {
+                    tmem_ld32(tO + cc * 32, o);
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 32; ++u) o[u] = 0u;
+                }
+                if (valid) {
+#pragma unroll
+                    for (int v = 0; v < 8; ++v) {
+                        const int c = cc * 32 + 4 * v;
+                        if (c < D) {
+                            float4 w = make_float4(u2f(o[4 * v]) * mult, u2f(o[4 * v + 1]) * mult,
+                                                   u2f(o[4 * v + 2]) * mult, u2f(o[4 * v + 3]) * mult);
+                            *reinterpret_cast<float4 *>(dst + c) = w;
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    // ---------------- teardown
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::TMEM_COLS);
+    }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+    return fn;
+}
+
+// 3-D bf16 tensor map with 128-byte swizzle: dims {d0 (contiguous), d1, d2}, byte strides of
+// d1 and d2, box {64, box1, 1}. Out-of-range elements read as zero.
+static bool make_map_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                        uint64_t s2, uint32_t box1) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {d0, d1, d2};
+    cuuint64_t strides[2] = {s1, s2};
+    cuuint32_t box[3] = {64, box1, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+template <int DP, int NQT, bool VT, bool PARTIAL>
+static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
+    using C = TcConfig<DP, NQT>;
+    auto kern = fa_tc_kernel<DP, NQT, VT, PARTIAL>;
+    static int attr_done[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return ATTN_ERR_CUDA;
+    if (dev < 64 && !attr_done[dev]) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+            return ATTN_ERR_CUDA;
+        attr_done[dev] = 1;
+    }
+    const int group = P->Hq / P->Hkv;
+    const uint64_t rows = (uint64_t)group * P->Sq;
+    const uint64_t D = (uint64_t)P->D;
+    CUtensorMap tmQ, tmK, tmV;
+    if (!make_map_3d(&tmQ, P->Q, D, rows, P->Hkv, D * 2, rows * D * 2, kBM)) return ATTN_ERR_CUDA;
+    if (!make_map_3d(&tmK, P->K, D, P->Sk, P->Hkv, D * 2, (uint64_t)P->Sk * D * 2, kBN)) return ATTN_ERR_CUDA;
+    if (!VT) {
+        if (!make_map_3d(&tmV, P->V, D, P->Sk, P->Hkv, D * 2, (uint64_t)P->Sk * D * 2, kBN)) return ATTN_ERR_CUDA;
+    } else {
+        if (!make_map_3d(&tmV, P->V, P->Sk, D, P->Hkv, (uint64_t)P->Sk * 2, (uint64_t)P->Sk * D * 2, DP))
+            return ATTN_ERR_CUDA;
+    }
+    TcParams prm;
+    prm.O = P->O;
+    prm.part_m = P->part_m;
+    prm.part_l = P->part_l;
+    prm.part_acc = P->part_acc;
+    prm.status = P->status;
+    prm.rows_per_kv = (int)rows;
+    prm.total_rows = P->Hq * P->Sq;
+    prm.Sq = P->Sq;
+    prm.Sk = P->Sk;
+    prm.Sk_total = P->Sk_total;
+    prm.k_begin = P->k_begin;
+    prm.D = P->D;
+    prm.causal = P->causal;
+    prm.keys_per_split = P->keys_per_split;
+    prm.scale_log2 = P->scale_log2;
+    dim3 grid(tiles_per_kv, P->Hkv, P->nsplit);
+    kern<<<grid, C::THREADS, C::SMEM, st>>>(tmQ, tmK, tmV, prm);
+    return cudaGetLastError() == cudaSuccess ? ATTN_OK : ATTN_ERR_CUDA;
+}
+
+static int nqt_for(const fa_problem *P) {
+    const long long rows = (long long)(P->Hq / P->Hkv) * P->Sq;
+    return rows > kBM ? 2 : 1;
+}
+
+}  // namespace ts
+
+extern "C" int ts_tc_supported(const fa_problem *P) {
+    if (P->D % 8 != 0 || P->D > 128 || P->D < 8) return 0;
+    if (P->v_prepacked && P->Sk % 8 != 0) return 0;
+    if (((uintptr_t)P->Q | (uintptr_t)P->K | (uintptr_t)P->V) & 15u) return 0;
+    const float *out = P->O ? P->O : P->part_acc;
+    if (((uintptr_t)out) & 15u) return 0;
+    if (ts::encode_fn() == nullptr) return 0;
+    return 1;
+}
+
+extern "C" int ts_tc_ctas_per_split(const fa_problem *P) {
+    const long long rows = (long long)(P->Hq / P->Hkv) * P->Sq;
+    const int nqt = ts::nqt_for(P);
+    const long long tiles = (rows + ts::kBM * nqt - 1) / (ts::kBM * nqt);
+    return (int)(tiles * P->Hkv);
+}
+
+extern "C" int ts_launch_tc(const fa_problem *P, void *stream, int partial) {
+    using namespace ts;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const long long rows = (long long)(P->Hq / P->Hkv) * P->Sq;
+    const int nqt = nqt_for(P);
+    const int tiles = (int)((rows + kBM * nqt - 1) / (kBM * nqt));
+    const int dp = P->D <= 64 ? 64 : 128;
+    const bool vt = P->v_prepacked != 0;
+#define TS_LAUNCH(DPV, NQTV)                                                                      \
+    do {                                                                                          \
+        if (vt) return partial ? launch_tc<DPV, NQTV, true, true>(P, st, tiles)                   \
+                               : launch_tc<DPV, NQTV, true, false>(P, st, tiles);                 \
+        return partial ? launch_tc<DPV, NQTV, false, true>(P, st, tiles)                          \
+                       : launch_tc<DPV, NQTV, false, false>(P, st, tiles);                        \
+    } while (0)
+    if (dp == 64) {
+        if (nqt == 2) TS_LAUNCH(64, 2);
+        TS_LAUNCH(64, 1);
+    }
+    if (nqt == 2) TS_LAUNCH(128, 2);
+    TS_LAUNCH(128, 1);
+#undef TS_LAUNCH
+}

@@ -1,0 +1,64 @@
+/* fa_launch.h -- the plain-C contract between the host layer (attn_flash.c) and the CUDA
+ * launchers (*.cu). The host layer validates arguments, plans the split-KV decomposition and
+ * carves the scratch block; the launchers build TMA descriptors and launch kernels. */
+#ifndef TS_FA_LAUNCH_H
+#define TS_FA_LAUNCH_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Scratch block layout (device memory, caller-owned, ATTN_SCRATCH_ALIGN-aligned):
+ *   [0, 256)                       int status word (+ padding)
+ *   [256, 256 + cap*4)             partial m   [nsplit][rows]
+ *   then                           partial l   [nsplit][rows]
+ *   then                           partial acc [nsplit][rows][D]
+ * where cap = ATTN_PARTIAL_ROWS, and the three regions are sized for D at the full cap. */
+#define TS_SCRATCH_CTRL_BYTES 256
+
+typedef struct fa_problem {
+    const uint16_t *Q, *K, *V; /* device pointers */
+    float *O;                  /* normalised output [Hq][Sq][D]; NULL in partial mode */
+    float *part_m, *part_l, *part_acc; /* where the kernel writes partials, [nsplit][Hq*Sq](,[D]) */
+    float *out_m, *out_l, *out_acc;    /* caller's single partial (write_partials mode) */
+    int *status;               /* device status word */
+    int Hq, Hkv, Sq, Sk;       /* Sk = keys present in K/V (local shard length) */
+    int Sk_total, k_begin;     /* global key axis length and this shard's first key */
+    int D, causal, v_prepacked;
+    int nsplit;                /* >1: split the key range, write partials, then combine */
+    int keys_per_split;        /* multiple of the key tile */
+    int write_partials;        /* 1: leave the result as (m, l, acc) partials, no combine */
+    float scale_log2;          /* (1/sqrt(D)) * log2(e) */
+} fa_problem;
+
+/* Number of SMs of the current device (cached). */
+int ts_num_sms(void);
+/* Compute capability major of the current device (cached). */
+int ts_cc_major(void);
+/* The tcgen05 path applies to this problem (D multiple of 8, <= 128, aligned pointers,
+ * Sk multiple of 8 when V is pre-transposed). Otherwise the SIMT path runs. */
+int ts_tc_supported(const fa_problem *p);
+/* CTAs the tcgen05 path launches per split for this problem (split planning input). */
+int ts_tc_ctas_per_split(const fa_problem *p);
+
+/* Launch the main kernel (tcgen05 or SIMT path chosen inside) plus, when nsplit > 1 and
+ * !write_partials, the combine kernel. Returns 0 or a negative ATTN_ERR_* code. */
+int ts_launch_attention(const fa_problem *p, void *stream);
+
+/* Launch the combine kernel alone on partial arrays. */
+int ts_launch_combine(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
+                      float *O, float *out_m, float *out_l, void *stream);
+
+/* Zero the device status word (async). */
+int ts_clear_status(int *status, void *stream);
+/* Synchronise the stream, read and clear the status word. */
+int ts_read_status(int *status, void *stream, int *value);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TS_FA_LAUNCH_H */
