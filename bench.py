@@ -1,0 +1,461 @@
+#!/usr/bin/env python
+"""bench.py -- benchmark of the B200 attention path (one JSON line on rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+Headline workload (the largest case): Qwen3-8B-shaped GQA prefill,
+Hq=32, Hkv=8, D=128, Sq=Sk=4096, non-causal, Q/K/V ~ N(0,1) seed 1 in bf16. A step is one
+attn_flash call over one sequence (batch 1 per GPU). Under torchrun each rank runs its own
+sequence -- the prefill shards by (batch x kv-head group) with no collective -- so the
+scaling is weak and `value` is the whole job's TFLOP/s.
+
+Keys of the JSON line beyond the base contract:
+  roofline      dominant kernel's achieved TFLOP/s (algorithmic FLOPs / CUDA-event time per
+                launch) against the measured bf16 peak in MEASURED_PEAKS.json, plus its DRAM
+                traffic per launch from the committed ncu summary (profiles/traffic.json)
+  cpu_baseline  the reference's own flash.c (oracle/_ref, compiled natively through the SVE
+                shim) timed on this host's cores on a bounded sample of the same workload
+  e2e           the same metric through the C ABI with pinned host buffers: every step copies
+                Q, K, V host->device and O device->host inside the timed region
+  decode        a secondary HBM-bound line: BASELINE config 3 (GQA decode, B=64, Sk=8192)
+  gpu_launches  kernels the library launched inside the timed region (its own counter)
+  clocks        SM clocks / throttle reasons sampled by NVML during the timed region
+
+--impl reference times the reference's CPU implementation of the path (oracle/_ref when
+present, else the oracle restatement) with all host threads on a bounded sample per step; under
+torchrun only rank 0 runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+METRIC = "attn TFLOP/s (prefill) and KV GB/s (decode) per GPU, % of roofline, 1/2/4/8"
+L2_BYTES = 126 * 1024 * 1024
+
+WORKLOADS = {
+    # name: (Hq, Hkv, Sq, Sk, D, causal, dist, seed, dist args, description)
+    "qwen3_gqa_prefill_s4096": (32, 8, 4096, 4096, 128, 0, "normal", 1, (0.0, 1.0),
+                                "BASELINE config 2: Qwen3-8B-shaped GQA prefill Hq32/Hkv8 D128 Sq=Sk=4096 non-causal"),
+    "qwen3_gqa_prefill_s2048": (32, 8, 2048, 2048, 128, 0, "normal", 1, (0.0, 1.0),
+                                "BASELINE config 2 at Sq=Sk=2048"),
+    "qwen3_gqa_prefill_s1024": (32, 8, 1024, 1024, 128, 0, "normal", 1, (0.0, 1.0),
+                                "BASELINE config 2 at Sq=Sk=1024"),
+    "mqa_prefill_b8_s2048": (8 * 16, 8, 2048, 2048, 128, 0, "uniform", 3, (-2.0, 2.0),
+                             "BASELINE config 4 prefill: MQA 16/1 D128 batch 8 Sq=Sk=2048"),
+    "gqa_decode_b64_sk8192": (64 * 32, 64 * 8, 1, 8192, 128, 0, "normal", 2, (0.0, 1.0),
+                              "BASELINE config 3: GQA decode B64 Hq32/Hkv8 D128 Sq=1 Sk=8192"),
+    "mqa_decode_b128_sk4096": (128 * 16, 128, 1, 4096, 128, 0, "uniform", 3, (-2.0, 2.0),
+                               "BASELINE config 4 decode: MQA 16/1 D128 batch 128 Sq=1 Sk=4096"),
+}
+DEFAULT_WORKLOAD = "qwen3_gqa_prefill_s4096"
+
+
+def flops(Hq, Sq, Sk, D, causal) -> float:
+    """4 * Hq * D * pairs (flash.c:1149 with attn_pairs, flash.c:874-887)."""
+    if not causal:
+        pairs = float(Sq) * Sk
+    else:
+        i = np.arange(Sq, dtype=np.float64)
+        pairs = float(np.clip(Sk - Sq + i + 1, 0, Sk).sum())
+    return 4.0 * Hq * D * pairs
+
+
+def algo_bytes(Hq, Hkv, Sq, Sk, D) -> float:
+    """Q, K, V read once in bf16 and O written once in fp32."""
+    return 2.0 * Hq * Sq * D + 2.0 * 2.0 * Hkv * Sk * D + 4.0 * Hq * Sq * D
+
+
+def is_decode(w) -> bool:
+    return w[2] == 1
+
+
+def host_inputs(w):
+    import oracle
+
+    Hq, Hkv, Sq, Sk, D, causal, dist, seed, (a, b), _ = w
+    return oracle.seeded_inputs(Hq, Hkv, Sq, Sk, D, seed=seed, dist=dist, a=a, b=b)
+
+
+def load_peaks() -> dict:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def load_traffic(workload: str):
+    p = REPO / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    e = d.get(workload)
+    return None if e is None else e.get("dram_bytes_per_launch")
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Polls SM clock and throttle reasons with NVML in a background thread."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+        "sync_boost": 0x10, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int):
+        self.samples = []
+        self.ok = False
+        self.max_mhz = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:  # noqa: BLE001 -- clocks are reported as unavailable
+            self.ok = False
+        self._stop = threading.Event()
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((time.perf_counter(), mhz, rs))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.002)
+
+    def start(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+
+    def stop(self):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self, t0: float, t1: float) -> dict:
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        inside = [s for s in self.samples if t0 <= s[0] <= t1]
+        if not inside:  # region shorter than one poll: take the sample nearest its middle
+            mid = 0.5 * (t0 + t1)
+            inside = [min(self.samples, key=lambda s: abs(s[0] - mid))]
+        mhz = sorted(s[1] for s in inside)
+        bits = 0
+        for s in inside:
+            bits |= s[2]
+        reasons = [k for k, v in self.REASONS.items() if bits & v and k != "gpu_idle"]
+        return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(inside)}
+
+
+# ------------------------------------------------------------------ CPU reference timing
+def cpu_reference_sample(w, seconds: float, threads: int | None = None) -> dict:
+    """Times the reference's own flash.c (oracle/_ref) -- or the oracle restatement when the
+    reference build is absent -- on a bounded sample of workload w: each host thread runs
+    attn_flash on its own (head, row-slice) with the workload's full key length. Non-causal
+    rows are independent, so a row slice is the same computation as in the full problem."""
+    import oracle
+
+    Hq, Hkv, Sq, Sk, D, causal, *_ = w
+    group = Hq // Hkv
+    threads = threads or os.cpu_count() or 1
+    use_ref = oracle.ref_available(128)
+    kind = "reference" if use_ref else "port"
+    Q, K, V = host_inputs(w)
+    rows = max(1, min(Sq, 8))
+
+    def task(t: int, nrows: int) -> float:
+        h = t % Hq
+        kv = h // group
+        r0 = (t * 97) % max(1, Sq - nrows + 1)
+        q = np.ascontiguousarray(Q.reshape(Hq, Sq, D)[h, r0:r0 + nrows])
+        k = np.ascontiguousarray(K.reshape(Hkv, Sk, D)[kv])
+        v = np.ascontiguousarray(V.reshape(Hkv, Sk, D)[kv])
+        if use_ref:
+            oracle.ref_attn_flash(q, k, v, 1, 1, nrows, Sk, D, causal, bk=128, bq=128)
+        else:
+            oracle.attn_blocked(q, k, v, 1, 1, nrows, Sk, D, causal, bk=128, bq=128, nthreads=1)
+        return flops(1, nrows, Sk, D, causal)
+
+    # calibrate the slice so that the timed sample takes ~`seconds`
+    t0 = time.perf_counter()
+    task(0, rows)
+    one = max(time.perf_counter() - t0, 1e-4)
+    rows = int(max(1, min(Sq, rows * seconds / one / 4)))
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        t0 = time.perf_counter()
+        fl = sum(ex.map(lambda t: task(t, rows), range(threads * 4)))
+        dt = time.perf_counter() - t0
+    return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": kind,
+            "sample": f"{threads * 4} tasks of 1 head x {rows} query rows x Sk={Sk} (D={D}) on {threads} threads, "
+                      f"{dt:.1f} s; non-causal rows are independent so a row slice is the full problem's work per row",
+            "seconds": dt}
+
+
+def run_reference(args, w) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+
+    Hq, Hkv, Sq, Sk, D, causal, *_ = w
+    threads = os.cpu_count() or 1
+    # size each step so that the whole run takes about a minute of CPU time
+    budget = 60.0 / max(1, args.steps + args.warmup)
+    for _ in range(args.warmup):
+        cpu_reference_sample(w, min(budget, 2.0), threads)
+    vals, secs = [], 0.0
+    for _ in range(args.steps):
+        r = cpu_reference_sample(w, budget, threads)
+        vals.append(r["value"])
+        secs += r["seconds"]
+    value = float(np.mean(vals))
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / max(1, args.steps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic " + w[9],
+        "config": {"workload": args.workload, "global_batch": 1, "seq_len": Sq, "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": r["kind"],
+                         "sample": r["sample"]},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ GPU timing
+def run_ours(args, w) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import transfer_station_b200 as ts
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            t = torch.zeros(1, device=dev)
+            dist.all_reduce(t)
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    ts.load_library()
+    Hq, Hkv, Sq, Sk, D, causal, *_ = w
+    decode = is_decode(w)
+    fl = flops(Hq, Sq, Sk, D, causal)
+    by = algo_bytes(Hq, Hkv, Sq, Sk, D)
+    Q, K, V = host_inputs(w)  # same seeded data on every rank; each rank owns its copy
+    set_bytes = Q.nbytes + K.nbytes + V.nbytes + Hq * Sq * D * 4
+    ncopy = max(1, -(-2 * L2_BYTES // set_bytes))  # rotating pool >= 2x L2: every step is L2-cold
+    qs = [torch.from_numpy(Q.view(np.int16)).to(dev) for _ in range(ncopy)]
+    ks = [torch.from_numpy(K.view(np.int16)).to(dev) for _ in range(ncopy)]
+    vs = [torch.from_numpy(V.view(np.int16)).to(dev) for _ in range(ncopy)]
+    os_ = [torch.empty(Hq * Sq * D, dtype=torch.float32, device=dev) for _ in range(ncopy)]
+    scratch = torch.empty(ts.attn_flash_scratch_bytes(D, 128), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i: int):
+        c = i % ncopy
+        rc = ts.attn_flash_stream(qs[c], ks[c], vs[c], os_[c], Hq, Hkv, Sq, Sk, D, causal, 128, scratch, 0, stream)
+        if rc != ts.ATTN_OK:
+            raise ts.AttnError(rc, "attn_flash_stream")
+
+    for i in range(args.warmup):
+        step(i)
+    rc, code = ts.attn_flash_status(scratch, stream)
+    if rc != ts.ATTN_OK:
+        raise ts.AttnError(rc, f"warmup device status {code}")
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    launches0 = ts.attn_flash_kernel_launches()
+    h0 = time.perf_counter()
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    h1 = time.perf_counter()
+    launches = ts.attn_flash_kernel_launches() - launches0
+    barrier()
+    clocks.stop()
+    rc, code = ts.attn_flash_status(scratch, stream)
+    if rc != ts.ATTN_OK:
+        raise ts.AttnError(rc, f"timed-region device status {code}")
+    ms_local = e0.elapsed_time(e1)
+    ms = max_over_ranks(ms_local)
+    ms_step = ms / args.steps
+    per_launch_ms = ms_local / args.steps
+    peaks = load_peaks()
+    if decode:
+        value = world * by * args.steps / (ms / 1e3) / 1e9
+        unit = "GB/s"
+        achieved = by / (per_launch_ms / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"]}
+    else:
+        value = world * fl * args.steps / (ms / 1e3) / 1e12
+        unit = "TFLOP/s"
+        achieved = fl / (per_launch_ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops"]}
+    roof["traffic"] = load_traffic(args.workload)
+    roof["algorithmic_per_launch"] = by if decode else fl
+    roof["peak_source"] = peaks["source"] + (" burst" if not decode else " copy")
+    roof["kernel"] = "ts::fa_tc_kernel (tcgen05 + TMA + TMEM)"
+
+    # ---------------- e2e through the C ABI with pinned host buffers
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    hq = torch.from_numpy(Q.view(np.int16)).pin_memory()
+    hk = torch.from_numpy(K.view(np.int16)).pin_memory()
+    hv = torch.from_numpy(V.view(np.int16)).pin_memory()
+    ho = torch.empty(Hq * Sq * D, dtype=torch.float32).pin_memory()
+    dq, dk, dv, do = qs[0], ks[0], vs[0], os_[0]
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        rc = ts.attn_flash_stream(dq, dk, dv, do, Hq, Hkv, Sq, Sk, D, causal, 128, scratch, 0, stream)
+        if rc != ts.ATTN_OK:
+            raise ts.AttnError(rc, "attn_flash_stream (e2e)")
+        ho.copy_(do, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_val = world * (by if decode else fl) * e2e_steps / (e2e_ms / 1e3) / (1e9 if decode else 1e12)
+    rc, code = ts.attn_flash_status(scratch, stream)
+    if rc != ts.ATTN_OK:
+        raise ts.AttnError(rc, f"e2e device status {code}")
+
+    # ---------------- secondary decode line (HBM-bound), single rank timing, max over ranks
+    decode_line = None
+    if not args.no_decode and not decode:
+        dw = WORKLOADS["gqa_decode_b64_sk8192"]
+        dHq, dHkv, dSq, dSk, dD, dc, *_ = dw
+        dQ, dK, dV = host_inputs(dw)
+        tq = torch.from_numpy(dQ.view(np.int16)).to(dev)
+        tk = torch.from_numpy(dK.view(np.int16)).to(dev)
+        tv = torch.from_numpy(dV.view(np.int16)).to(dev)
+        to = torch.empty(dHq * dD, dtype=torch.float32, device=dev)
+        dsteps = max(3, min(args.steps, 200))
+        for _ in range(3):
+            ts.attn_flash_stream(tq, tk, tv, to, dHq, dHkv, dSq, dSk, dD, dc, 128, scratch, 0, stream)
+        barrier()
+        e0.record(stream)
+        for _ in range(dsteps):
+            ts.attn_flash_stream(tq, tk, tv, to, dHq, dHkv, dSq, dSk, dD, dc, 128, scratch, 0, stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        dms = max_over_ranks(e0.elapsed_time(e1)) / dsteps
+        dby = algo_bytes(dHq, dHkv, dSq, dSk, dD)
+        rc, code = ts.attn_flash_status(scratch, stream)
+        if rc != ts.ATTN_OK:
+            raise ts.AttnError(rc, f"decode device status {code}")
+        dach = dby / (dms / 1e3) / 1e9
+        decode_line = {"workload": "gqa_decode_b64_sk8192", "desc": dw[9], "value": world * dach, "unit": "GB/s",
+                       "per_gpu_gbs": dach, "ms_per_step": dms, "frac_of_measured_hbm": dach / peaks["hbm_gbs"],
+                       "frac_of_8tbs_spec": dach / 8000.0, "bytes_per_step": dby, "steps": dsteps,
+                       "l2": "K+V = 2 GiB per step > L2"}
+        del tq, tk, tv, to
+
+    # ---------------- CPU baseline (rank 0, N=1 only)
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        r = cpu_reference_sample(w, args.cpu_seconds)
+        cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+
+    csum = clocks.summary(h0, h1)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": f"synthetic, seeded ({w[6]}, seed {w[7]}), bf16 RNE; {w[9]}",
+            "config": {"workload": args.workload, "global_batch": world, "seq_len": Sq, "Hq": Hq,
+                       "Hkv": Hkv, "head_dim": D, "causal": bool(causal),
+                       "parallelism": f"dp{world} (one sequence per GPU, sharded by batch x kv-head group, no collective)",
+                       "l2": f"rotating pool of {ncopy} Q/K/V/O sets ({ncopy * set_bytes / 2**20:.0f} MiB >= 2x L2)"},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": int(Q.nbytes + K.nbytes + V.nbytes),
+                    "d2h_bytes_per_step": int(Hq * Sq * D * 4), "steps": e2e_steps,
+                    "path": "pinned host -> cudaMemcpyAsync -> attn_flash_stream -> cudaMemcpyAsync -> pinned host"},
+            "gpu_launches": int(launches),
+            "clocks": csum,
+            "decode": decode_line,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
+    ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    w = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference(args, w)
+    else:
+        run_ours(args, w)
+
+
+if __name__ == "__main__":
+    main()

@@ -107,6 +107,11 @@ int attn_flash_status(void *scratch, void *stream, int *device_code);
 /* Human-readable name of a status code. */
 const char *attn_flash_strerror(int status);
 
+/* Diagnostic: number of CUDA kernels this library has launched in this process (all
+ * devices, all entry points). No counterpart in flash.c; benchmarks use it to report how
+ * many of the library's kernels ran inside a timed region. */
+unsigned long long attn_flash_kernel_launches(void);
+
 /* Key-sharded partial attention for multi-GPU long-context decode (no counterpart in
  * flash.c, whose single call covers all keys; this is the per-GPU half of the key split
  * of flash.c:798's key loop). K and V hold keys [k_begin, k_begin + Sk_local) of a key

@@ -43,6 +43,7 @@ EXPORTS = {
                                                                                           ctypes.c_void_p]),
     "attn_flash_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
     "attn_flash_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "attn_flash_kernel_launches": (ctypes.c_ulonglong, []),
     "attn_flash_partial_stream": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 10 +
                                   [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "attn_flash_combine_stream": (ctypes.c_int, [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
@@ -80,6 +81,10 @@ def load_library(path: os.PathLike | str | None = None) -> ctypes.CDLL:
 
 def strerror(status: int) -> str:
     return load_library().attn_flash_strerror(status).decode()
+
+
+def attn_flash_kernel_launches() -> int:
+    return int(load_library().attn_flash_kernel_launches())
 
 
 def attn_flash_scratch_bytes(D: int, bk: int) -> int:

@@ -10,10 +10,20 @@
 #include <math.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "attn_flash.h"
 #include "fa_launch.h"
 
 extern "C" int ts_launch_tc(const fa_problem *P, void *stream, int partial);
+
+static std::atomic<unsigned long long> g_kernel_launches{0};
+
+extern "C" void ts_count_launch(void) { g_kernel_launches.fetch_add(1, std::memory_order_relaxed); }
+
+extern "C" unsigned long long attn_flash_kernel_launches(void) {
+    return g_kernel_launches.load(std::memory_order_relaxed);
+}
 
 namespace ts {
 
@@ -171,7 +181,9 @@ extern "C" int ts_launch_combine(const float *m, const float *l, const float *ac
     dim3 grid((rows + warps - 1) / warps);
     ts::fa_combine_kernel<<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows, D, O,
                                                                                       out_m, out_l);
-    return cudaGetLastError() == cudaSuccess ? ATTN_OK : ATTN_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
+    ts_count_launch();
+    return ATTN_OK;
 }
 
 static int launch_simt(const fa_problem *P, void *stream, int partial) {
@@ -199,7 +211,9 @@ static int launch_simt(const fa_problem *P, void *stream, int partial) {
     const int warps = 8;
     dim3 grid((unsigned)((rows + warps - 1) / warps), P->nsplit);
     ts::fa_simt_kernel<<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(s);
-    return cudaGetLastError() == cudaSuccess ? ATTN_OK : ATTN_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
+    ts_count_launch();
+    return ATTN_OK;
 }
 
 extern "C" int ts_launch_attention(const fa_problem *P, void *stream) {

@@ -43,6 +43,8 @@
 #include "fa_launch.h"
 #include "sm100_ptx.cuh"
 
+extern "C" void ts_count_launch(void);
+
 namespace ts {
 
 constexpr int kBM = 128;              // query rows per tile (TMEM lanes)
@@ -508,7 +510,9 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     prm.scale_log2 = P->scale_log2;
     dim3 grid(tiles_per_kv, P->Hkv, P->nsplit);
     kern<<<grid, C::THREADS, C::SMEM, st>>>(tmQ, tmK, tmV, prm);
-    return cudaGetLastError() == cudaSuccess ? ATTN_OK : ATTN_ERR_CUDA;
+    if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
+    ts_count_launch();
+    return ATTN_OK;
 }
 
 static int nqt_for(const fa_problem *P) {
