@@ -1,0 +1,118 @@
+"""CPU: the C-ABI library's host side -- it loads, exports every symbol the header declares,
+keeps the reference's bk contract (abort at both doors, flash.c:641-647), sizes scratch
+independently of Sq/Sk (flash.c:679-682), picks bk with the reference's model
+(README.md:359-436), and validates arguments before touching the GPU."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+import oracle
+import transfer_station_b200 as ts
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "attn_flash.h"
+
+
+def declared_functions() -> set[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return set(re.findall(r"\b(attn_flash\w*)\s*\(", text))
+
+
+def test_library_exports_every_declared_symbol(built_lib):
+    names = declared_functions()
+    assert {"attn_flash", "attn_flash_scratch_bytes", "attn_flash_pick_bk"} <= names
+    for n in names:
+        assert hasattr(built_lib, n), n
+    assert names == set(ts.EXPORTS), "the Python mirror binds exactly the declared symbols"
+
+
+def test_library_has_sm100a_code(built_lib):
+    """The .so carries sm_100a device code (cuobjdump --list-elf only names the embedded images)."""
+    res = subprocess.run(["cuobjdump", "--list-elf", str(ts.LIB_PATH)], capture_output=True, text=True)
+    assert res.returncode == 0 and "sm_100a" in res.stdout
+
+
+def _abort_run(code: str) -> subprocess.CompletedProcess:
+    return subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, cwd=REPO)
+
+
+@pytest.mark.parametrize("bk", [0, -16, 8, 100, 8192, 48])
+def test_bad_bk_aborts_scratch_bytes(built_lib, bk):
+    r = _abort_run(f"import transfer_station_b200 as t; t.attn_flash_scratch_bytes(128, {bk})")
+    assert r.returncode < 0  # SIGABRT
+    assert f"attn_flash_scratch_bytes: bk={bk} is invalid" in r.stderr and "POWER OF TWO in [16, 4096]" in r.stderr
+
+
+def test_bad_bk_aborts_attn_flash(built_lib):
+    """The second door: the attention entry itself re-checks bk before anything else."""
+    r = _abort_run("import transfer_station_b200 as t; t.load_library().attn_flash_stream("
+                   "None, None, None, None, 4, 4, 8, 8, 64, 0, 100, None, 0, None)")
+    assert r.returncode < 0 and "attn_flash: bk=100 is invalid" in r.stderr
+
+
+@pytest.mark.parametrize("bk", [16, 32, 64, 128, 256, 512, 1024, 2048, 4096])
+def test_scratch_bytes_contract(built_lib, bk):
+    s128 = ts.attn_flash_scratch_bytes(128, bk)
+    assert s128 % ts.ATTN_SCRATCH_ALIGN == 0
+    assert s128 >= 256 + ts.ATTN_PARTIAL_ROWS * (128 + 2) * 4
+    assert ts.attn_flash_scratch_bytes(64, bk) < s128 < ts.attn_flash_scratch_bytes(256, bk)
+
+
+def test_pick_bk_is_reference_model_capped_at_gpu_tile(built_lib):
+    MiB = 1 << 20
+    for D in (1, 8, 40, 64, 128, 256, 512, 2**31 - 1):
+        for l2 in (0, 1, 4096, MiB, 8 * MiB, 126 * MiB, 2**63):
+            want = min(oracle.pick_bk_model(D, l2, 128), ts.ATTN_GPU_KEY_TILE)
+            got = ts.attn_flash_pick_bk(D, l2)
+            assert got == want, (D, l2)
+            assert got & (got - 1) == 0 and ts.ATTN_BK_MIN <= got <= ts.ATTN_GPU_KEY_TILE
+    assert ts.attn_flash_pick_bk(-5, MiB) == ts.attn_flash_pick_bk(1, MiB)  # D < 1 clamped
+
+
+def _lib_call(**kw):
+    a = dict(Q=1 << 20, K=1 << 20, V=1 << 20, O=1 << 20, Hq=8, Hkv=2, Sq=16, Sk=16, D=64, causal=0, bk=128,
+             scratch=1 << 20, vp=0)
+    a.update(kw)
+    return ts.load_library().attn_flash_stream(a["Q"], a["K"], a["V"], a["O"], a["Hq"], a["Hkv"], a["Sq"], a["Sk"],
+                                               a["D"], a["causal"], a["bk"], a["scratch"], a["vp"], None)
+
+
+@pytest.mark.parametrize("bad", [dict(Q=0), dict(O=0), dict(scratch=0), dict(Hq=6, Hkv=4), dict(Hkv=0),
+                                 dict(Sq=0), dict(Sk=0), dict(D=0), dict(D=257)])
+def test_argument_validation_before_any_gpu_work(built_lib, bad):
+    assert _lib_call(**bad) == ts.ATTN_ERR_ARGS
+
+
+def test_misaligned_scratch(built_lib):
+    assert _lib_call(scratch=(1 << 20) + 4) == ts.ATTN_ERR_ALIGN
+
+
+def test_no_b200_is_reported_not_faked(built_lib):
+    """Without a compute-capability-10 device the call returns a status -- there is no CPU
+    fallback path."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert _lib_call() == ts.ATTN_ERR_NOT_SM100
+
+
+def test_strerror(built_lib):
+    for code in (ts.ATTN_OK, ts.ATTN_ERR_ARGS, ts.ATTN_ERR_ALIGN, ts.ATTN_ERR_CUDA, ts.ATTN_ERR_DEVICE,
+                 ts.ATTN_ERR_NOT_SM100):
+        assert ts.strerror(code) and ts.strerror(code) != "unknown status"
+    assert ts.strerror(12345) == "unknown status"
+
+
+def test_missing_library_raises_no_fallback(tmp_path):
+    with pytest.raises(FileNotFoundError):
+        ts.load_library(tmp_path / "nope.so")
+
+
+def test_kernel_launch_counter_starts_at_zero(built_lib):
+    assert isinstance(ts.attn_flash_kernel_launches(), int)

@@ -172,9 +172,9 @@ static int ts_run(fa_problem *p, void *scratch, void *stream) {
 int attn_flash_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O, int Hq, int Hkv, int Sq,
                       int Sk, int D, int causal, int bk, void *scratch, int v_prepacked, void *stream) {
     attn_bk_check(bk, "attn_flash");
+    if (!O) return ATTN_ERR_ARGS;
     int rc = ts_validate(Q, K, V, Hq, Hkv, Sq, Sk, D, scratch);
     if (rc != ATTN_OK) return rc;
-    if (!O) return ATTN_ERR_ARGS;
     fa_problem p;
     ts_fill(&p, Q, K, V, Hq, Hkv, Sq, Sk, D, causal, v_prepacked);
     p.O = O;
@@ -185,9 +185,9 @@ int attn_flash_partial_stream(const uint16_t *Q, const uint16_t *K, const uint16
                               float *acc, int Hq, int Hkv, int Sq, int Sk_local, int Sk_total, int k_begin, int D,
                               int causal, int bk, void *scratch, int v_prepacked, void *stream) {
     attn_bk_check(bk, "attn_flash_partial");
+    if (!m || !l || !acc || k_begin < 0 || Sk_total < (long long)k_begin + Sk_local) return ATTN_ERR_ARGS;
     int rc = ts_validate(Q, K, V, Hq, Hkv, Sq, Sk_local, D, scratch);
     if (rc != ATTN_OK) return rc;
-    if (!m || !l || !acc || k_begin < 0 || Sk_total < (long long)k_begin + Sk_local) return ATTN_ERR_ARGS;
     fa_problem p;
     ts_fill(&p, Q, K, V, Hq, Hkv, Sq, Sk_local, D, causal, v_prepacked);
     p.Sk_total = Sk_total;
