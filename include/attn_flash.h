@@ -131,6 +131,19 @@ int attn_flash_partial_stream(const uint16_t *Q, const uint16_t *K, const uint16
 int attn_flash_combine_stream(const float *m, const float *l, const float *acc, int nparts,
                               int rows, int D, float *O, void *stream);
 
+/* attn_flash without a scratch argument, for callers that cannot allocate device memory (a
+ * host whose device memory belongs to its own pool allocator, or a foreign-function binding
+ * with nowhere to keep a device buffer between calls). No counterpart in the reference: its
+ * scratch is host memory the caller passes in. Uses a fixed 4 MiB block of device memory
+ * declared by the library (held on every GPU that loads it until exit) and calls no
+ * allocator. Accepts at most 4096 query rows (Hq*Sq) -- decode-shaped calls -- and returns
+ * ATTN_ERR_ARGS beyond that. All calls on a device share the block: calls whose GPU work
+ * overlaps race. The first call on a device looks the block up (make it before any stream
+ * capture). Blocks until the work on `stream` is done; returns ATTN_OK or a status code. */
+int attn_flash_noalloc(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O, int Hq,
+                       int Hkv, int Sq, int Sk, int D, int causal, int bk, int v_prepacked,
+                       void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -48,6 +48,7 @@ EXPORTS = {
                                   [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "attn_flash_combine_stream": (ctypes.c_int, [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                  _f32p, ctypes.c_void_p]),
+    "attn_flash_noalloc": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 8 + [ctypes.c_void_p]),
 }
 
 _lib = None
@@ -145,6 +146,13 @@ def attn_flash_partial_stream(Q, K, V, m, l, acc, Hq, Hkv, Sq, Sk_local, Sk_tota
     return int(load_library().attn_flash_partial_stream(_ptr(Q), _ptr(K), _ptr(V), _ptr(m), _ptr(l), _ptr(acc), Hq,
                                                         Hkv, Sq, Sk_local, Sk_total, k_begin, D, int(causal), bk,
                                                         _ptr(scratch), int(v_prepacked), _stream_handle(stream)))
+
+
+def attn_flash_noalloc(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, v_prepacked=0, stream=None) -> int:
+    """attn_flash for callers that cannot allocate: no scratch argument (the library's own
+    fixed 4 MiB device block is used), at most 4096 query rows, blocking. Returns the status."""
+    return int(load_library().attn_flash_noalloc(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), Hq, Hkv, Sq, Sk, D, int(causal),
+                                                 bk, int(v_prepacked), _stream_handle(stream)))
 
 
 def attn_flash_combine_stream(m, l, acc, nparts, rows, D, O, stream=None) -> int:
