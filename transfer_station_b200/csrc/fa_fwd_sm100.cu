@@ -168,6 +168,11 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
+    // Register budgets per warpgroup (NQT=2 launches 384 threads x 168 registers): the
+    // producer/MMA warpgroup gives registers up, the two softmax warpgroups take them:
+    // 128 x 56 + 256 x 224 = 64512 = 384 x 168.
+    if (warp < 4) {
+        if constexpr (NQT == 2) regs_dec<112>();
     if (warp == 0) {
         // ============================ TMA producer
         if (lane == 0 && nblk > 0) {
@@ -288,7 +293,17 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             drain_wait(done_bar, 0, p.status);
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    }
+        // teardown (producer/MMA warpgroup): every TMEM user has fenced, then warp 1 frees TMEM
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 1) {
+            __syncwarp();
+            tc_fence_after();
+            tmem_dealloc(tmem_base, C::TMEM_COLS);
+        }
+    } else {
+        if constexpr (NQT == 2) regs_inc<192>();
         // ============================ softmax / correction / epilogue
         const int t = (warp - 4) >> 2;
         const int quad = warp & 3;
@@ -311,53 +326,89 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
-            uint32_t sa[32], sb[32], sc[32], sd[32];
-            tmem_ld32x2(tS, tS + 32, sa, sb);
-            tmem_ld32x2(tS + 64, tS + 96, sc, sd);
-            float f[128];
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-                f[c] = u2f(sa[c]);
-                f[32 + c] = u2f(sb[c]);
-                f[64 + c] = u2f(sc[c]);
-                f[96 + c] = u2f(sd[c]);
-            }
+            uint32_t sr[128];
+            tmem_ld128(tS, sr);
             const long long key0 = kb0 + (long long)j * kBN;
             const long long nv = lastkey - key0 + 1;
-            if (nv < kBN) {
+            // `full`: every row of this warp sees every key of the block (no tail, no causal
+            // cut); then the warp takes the fast path below, else the exact masked path. The
+            // choice must be warp-uniform: both paths issue warp-collective tcgen05.st.
+            const bool full = __all_sync(0xffffffffu, nv >= kBN);
+            float mb;
+            if (full) {
+                float mx[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) mx[k] = fmax3(u2f(sr[k]), u2f(sr[8 + k]), u2f(sr[16 + k]));
+#pragma unroll
+                for (int c = 24; c < 128; c += 16)
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) mx[k] = fmax3(mx[k], u2f(sr[c + k]), u2f(sr[c + 8 + k]));
+                mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
+            } else {
                 const int nvalid = nv < 0 ? 0 : (int)nv;
 #pragma unroll
                 for (int c = 0; c < 128; ++c)
-                    if (c >= nvalid) f[c] = -INFINITY;
-            }
-            float mx0 = f[0], mx1 = f[1], mx2 = f[2], mx3 = f[3];
+                    if (c >= nvalid) sr[c] = f2u(-INFINITY);
+                float mx0 = u2f(sr[0]), mx1 = u2f(sr[1]), mx2 = u2f(sr[2]), mx3 = u2f(sr[3]);
 #pragma unroll
-            for (int c = 4; c < 128; c += 4) {
-                mx0 = fmaxf(mx0, f[c]);
-                mx1 = fmaxf(mx1, f[c + 1]);
-                mx2 = fmaxf(mx2, f[c + 2]);
-                mx3 = fmaxf(mx3, f[c + 3]);
+                for (int c = 4; c < 128; c += 4) {
+                    mx0 = fmaxf(mx0, u2f(sr[c]));
+                    mx1 = fmaxf(mx1, u2f(sr[c + 1]));
+                    mx2 = fmaxf(mx2, u2f(sr[c + 2]));
+                    mx3 = fmaxf(mx3, u2f(sr[c + 3]));
+                }
+                mb = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
             }
-            const float mb = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
             float m_new = m;
             if (mb > m && (m == -INFINITY || (mb - m) * sl2 > kRescaleLog2)) m_new = mb;
             const float alpha = (m_new == m) ? 1.f : ((m == -INFINITY) ? 0.f : ex2((m - m_new) * sl2));
             const float ms = (m_new == -INFINITY) ? 0.f : __fmul_rn(m_new, sl2);
             float rs0 = 0.f, rs1 = 0.f;
+            if (full) {
+                // P = 2^(s*c - m*c) by one packed FMA per pair; 3 of every 8 pairs take the
+                // polynomial exp2 on the FMA pipe, the rest the MUFU unit, so both run at once.
+                const float2 c2 = make_float2(sl2, sl2), nms2 = make_float2(-ms, -ms);
+                float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int cc = 0; cc < 4; ++cc) {
-                uint32_t pk[16];
+                for (int cc = 0; cc < 4; ++cc) {
+                    uint32_t pk[16];
 #pragma unroll
-                for (int u = 0; u < 16; ++u) {
-                    // Rounded multiply, then subtract (never fused): the row's max element
-                    // gives exactly 2^0 = 1, as exp(S - m) does in flash.c:566.
-                    const float p0 = ex2(__fsub_rn(__fmul_rn(f[32 * cc + 2 * u], sl2), ms));
-                    const float p1 = ex2(__fsub_rn(__fmul_rn(f[32 * cc + 2 * u + 1], sl2), ms));
-                    rs0 += p0;
-                    rs1 += p1;
-                    pk[u] = pack_bf16x2(p0, p1);
+                    for (int u = 0; u < 16; ++u) {
+                        const float2 x = __ffma2_rn(make_float2(u2f(sr[32 * cc + 2 * u]), u2f(sr[32 * cc + 2 * u + 1])),
+                                                    c2, nms2);
+                        float2 pr;
+                        if ((u & 7) < 3) {
+                            pr = exp2_fma2(x);
+                        } else {
+                            pr.x = ex2(x.x);
+                            pr.y = ex2(x.y);
+                        }
+                        if (u & 1)
+                            acc1 = __fadd2_rn(acc1, pr);
+                        else
+                            acc0 = __fadd2_rn(acc0, pr);
+                        pk[u] = pack_bf16x2(pr.x, pr.y);
+                    }
+                    tmem_st16(tS + cc * 16, pk);
                 }
-                tmem_st16(tS + cc * 16, pk);
+                rs0 = acc0.x + acc1.x;
+                rs1 = acc0.y + acc1.y;
+            } else {
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) {
+                        // Rounded multiply, then subtract (never fused): the row's max element
+                        // gives exactly 2^0 = 1, as exp(S - m) does in flash.c:566.
+                        const float p0 = ex2(__fsub_rn(__fmul_rn(u2f(sr[32 * cc + 2 * u]), sl2), ms));
+                        const float p1 = ex2(__fsub_rn(__fmul_rn(u2f(sr[32 * cc + 2 * u + 1]), sl2), ms));
+                        rs0 += p0;
+                        rs1 += p1;
+                        pk[u] = pack_bf16x2(p0, p1);
+                    }
+                    tmem_st16(tS + cc * 16, pk);
+                }
             }
             l = l * alpha + (rs0 + rs1);
             m = m_new;
@@ -423,15 +474,9 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 }
             }
         }
-    }
-
-    // ---------------- teardown
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 1) {
-        __syncwarp();
-        tc_fence_after();
-        tmem_dealloc(tmem_base, C::TMEM_COLS);
+        // teardown (softmax warpgroups): TMEM reads done before the dealloc below
+        tc_fence_before();
+        __syncthreads();
     }
 }
 

@@ -206,6 +206,38 @@ __device__ __forceinline__ void tmem_ld32x2(uint32_t taddr, uint32_t taddr2, uin
         : "memory");
 }
 
+// All 128 columns [col, col+128) of this thread's lane in one load, then one wait.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&q)[128]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x128.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,"
+        "%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,"
+        "%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63,%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,"
+        "%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95,%96,%97,%98,%99,%100,%101,"
+        "%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,"
+        "%122,%123,%124,%125,%126,%127}, [%128];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(q[0]), "=r"(q[1]), "=r"(q[2]), "=r"(q[3]), "=r"(q[4]), "=r"(q[5]), "=r"(q[6]), "=r"(q[7]),
+          "=r"(q[8]), "=r"(q[9]), "=r"(q[10]), "=r"(q[11]), "=r"(q[12]), "=r"(q[13]), "=r"(q[14]), "=r"(q[15]),
+          "=r"(q[16]), "=r"(q[17]), "=r"(q[18]), "=r"(q[19]), "=r"(q[20]), "=r"(q[21]), "=r"(q[22]), "=r"(q[23]),
+          "=r"(q[24]), "=r"(q[25]), "=r"(q[26]), "=r"(q[27]), "=r"(q[28]), "=r"(q[29]), "=r"(q[30]), "=r"(q[31]),
+          "=r"(q[32]), "=r"(q[33]), "=r"(q[34]), "=r"(q[35]), "=r"(q[36]), "=r"(q[37]), "=r"(q[38]), "=r"(q[39]),
+          "=r"(q[40]), "=r"(q[41]), "=r"(q[42]), "=r"(q[43]), "=r"(q[44]), "=r"(q[45]), "=r"(q[46]), "=r"(q[47]),
+          "=r"(q[48]), "=r"(q[49]), "=r"(q[50]), "=r"(q[51]), "=r"(q[52]), "=r"(q[53]), "=r"(q[54]), "=r"(q[55]),
+          "=r"(q[56]), "=r"(q[57]), "=r"(q[58]), "=r"(q[59]), "=r"(q[60]), "=r"(q[61]), "=r"(q[62]), "=r"(q[63]),
+          "=r"(q[64]), "=r"(q[65]), "=r"(q[66]), "=r"(q[67]), "=r"(q[68]), "=r"(q[69]), "=r"(q[70]), "=r"(q[71]),
+          "=r"(q[72]), "=r"(q[73]), "=r"(q[74]), "=r"(q[75]), "=r"(q[76]), "=r"(q[77]), "=r"(q[78]), "=r"(q[79]),
+          "=r"(q[80]), "=r"(q[81]), "=r"(q[82]), "=r"(q[83]), "=r"(q[84]), "=r"(q[85]), "=r"(q[86]), "=r"(q[87]),
+          "=r"(q[88]), "=r"(q[89]), "=r"(q[90]), "=r"(q[91]), "=r"(q[92]), "=r"(q[93]), "=r"(q[94]), "=r"(q[95]),
+          "=r"(q[96]), "=r"(q[97]), "=r"(q[98]), "=r"(q[99]), "=r"(q[100]), "=r"(q[101]), "=r"(q[102]),
+          "=r"(q[103]), "=r"(q[104]), "=r"(q[105]), "=r"(q[106]), "=r"(q[107]), "=r"(q[108]), "=r"(q[109]),
+          "=r"(q[110]), "=r"(q[111]), "=r"(q[112]), "=r"(q[113]), "=r"(q[114]), "=r"(q[115]), "=r"(q[116]),
+          "=r"(q[117]), "=r"(q[118]), "=r"(q[119]), "=r"(q[120]), "=r"(q[121]), "=r"(q[122]), "=r"(q[123]),
+          "=r"(q[124]), "=r"(q[125]), "=r"(q[126]), "=r"(q[127])
+        : "r"(taddr)
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
@@ -232,11 +264,53 @@ __device__ __forceinline__ void tmem_wait_st() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
+// Per-warpgroup register budget changes (every warp of the warpgroup executes the same one).
+// The budgets of all warpgroups must add up to at most the block's launch allocation.
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // Hardware base-2 exponential (MUFU). ex2.approx(-inf) = +0.
 __device__ __forceinline__ float ex2(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// max(a, b, c) in one instruction (sm_100 three-input max).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// 2^x for two values on the FMA pipe instead of the MUFU unit (which is the softmax's
+// bottleneck when every exponential goes through it). Method: round-to-nearest range
+// reduction x = n + f, f in [-1/2, 1/2], done with the 1.5*2^23 shift (t = x + 1.5*2^23 holds
+// n in its low mantissa bits); 2^f by a degree-3 polynomial with constant term exactly 1 and
+// coefficients fitted (numpy, iteratively reweighted least squares toward minimax relative
+// error) over [-1/2, 1/2], max relative error 1.0e-4 -- 20x below the bf16 rounding that P
+// gets next; 2^n applied by adding n to the exponent field (bits(t) << 23 == n << 23 mod
+// 2^32). Inputs are clamped at -125 so the result stays a normal float (2^-125 ~ 2e-38 where
+// the exact value is smaller: irrelevant next to a denominator >= 1).
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+    constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
+    constexpr float c1 = 0.6932829022407532f, c2 = 0.24221020936965942f, c3 = 0.05500861629843712f;
+    x.x = fmaxf(x.x, -125.f);
+    x.y = fmaxf(x.y, -125.f);
+    const float2 t = __fadd2_rn(x, make_float2(kShift, kShift));
+    const float2 n = __fadd2_rn(t, make_float2(-kShift, -kShift));
+    const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+    float2 p = __ffma2_rn(make_float2(c3, c3), f, make_float2(c2, c2));
+    p = __ffma2_rn(p, f, make_float2(c1, c1));
+    p = __ffma2_rn(p, f, make_float2(1.f, 1.f));
+    return make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                       __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 
 // Two floats -> packed bf16x2, round-to-nearest-even; `lo` lands in bits [15:0].
