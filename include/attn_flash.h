@@ -51,7 +51,7 @@ extern "C" {
 /* Decode partial rows the scratch block holds (split-KV partials (m, l, acc[D])).
  * Scratch size stays independent of Sq and Sk, as in flash.c; a call whose split-KV plan
  * would need more partial rows uses fewer splits. */
-#define ATTN_PARTIAL_ROWS 32768
+#define ATTN_PARTIAL_ROWS 65536
 
 /* Status codes of the *_stream entry points. */
 #define ATTN_OK 0

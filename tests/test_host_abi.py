@@ -32,6 +32,24 @@ def test_library_exports_every_declared_symbol(built_lib):
     assert names == set(ts.EXPORTS), "the Python mirror binds exactly the declared symbols"
 
 
+def declared_arity() -> dict[str, int]:
+    """Parameter count of every function prototype in the header."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(attn_flash\w*)\s*\(([^)]*)\)\s*;", text):
+        params = params.strip()
+        out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_python_bindings_match_header_arity():
+    """Every ctypes signature in the Python mirror takes exactly the header's parameters."""
+    arity = declared_arity()
+    assert set(arity) == set(ts.EXPORTS)
+    for name, (_, args) in ts.EXPORTS.items():
+        assert len(args) == arity[name], (name, len(args), arity[name])
+
+
 def test_library_has_sm100a_code(built_lib):
     """The .so carries sm_100a device code (cuobjdump --list-elf only names the embedded images)."""
     res = subprocess.run(["cuobjdump", "--list-elf", str(ts.LIB_PATH)], capture_output=True, text=True)

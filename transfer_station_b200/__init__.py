@@ -21,7 +21,7 @@ ATTN_BK_DEFAULT = 128
 ATTN_SCRATCH_ALIGN = 256
 ATTN_GPU_KEY_TILE = 128
 ATTN_D_MAX = 256
-ATTN_PARTIAL_ROWS = 32768
+ATTN_PARTIAL_ROWS = 65536
 
 ATTN_OK = 0
 ATTN_ERR_ARGS = -1
@@ -44,7 +44,7 @@ EXPORTS = {
     "attn_flash_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
     "attn_flash_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "attn_flash_kernel_launches": (ctypes.c_ulonglong, []),
-    "attn_flash_partial_stream": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 10 +
+    "attn_flash_partial_stream": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p, _f32p, _f32p] + [ctypes.c_int] * 9 +
                                   [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "attn_flash_combine_stream": (ctypes.c_int, [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                  _f32p, ctypes.c_void_p]),

@@ -88,14 +88,22 @@ const char *attn_flash_strerror(int status) {
     }
 }
 
-/* Split-KV plan: pick nsplit minimising the modelled makespan
+/* Work plan. First the split-KV plan for problems with few CTAs (decode): pick nsplit
+ * minimising the modelled makespan
  *   T(s) = ceil(ctas*s / SMs) * (blocks/s + 1)
  * (the +1 is the per-CTA prologue/epilogue, in key-block units), subject to the partial
- * rows fitting the scratch and every split keeping >= 2 key blocks. */
-static void ts_plan_splits(fa_problem *p, int ctas) {
+ * rows fitting the scratch and every split keeping >= 2 key blocks. Otherwise, on the
+ * tensor-core path without causal masking, the tail wave: when the last wave of CTAs would
+ * run at most half full, its L units are split into floor(SMs / L) key pieces, so the last
+ * wave takes a fraction of a full CTA's time; their partials are merged afterwards. */
+static void ts_plan(fa_problem *p) {
+    const int tc = ts_tc_supported(p);
     const long long rows = (long long)p->Hq * p->Sq;
     const int nblk = (p->Sk + ATTN_GPU_KEY_TILE - 1) / ATTN_GPU_KEY_TILE;
-    const int sms = ts_num_sms();
+    const int sms = ts_num_sms() > 0 ? ts_num_sms() : 1;
+    const int ctas = tc ? ts_tc_ctas_per_split(p) : (int)((rows + 7) / 8);
+    p->n_direct = 0;
+    p->row_base = 0;
     long long cap = rows > 0 ? (long long)ATTN_PARTIAL_ROWS / rows : 0;
     int smax = nblk / 2;
     if (smax > cap) smax = (int)cap;
@@ -107,16 +115,32 @@ static void ts_plan_splits(fa_problem *p, int ctas) {
         const int seff = (nblk + bps - 1) / bps;
         if (seff != s) continue; /* same plan as a smaller s */
         const long long tot = (long long)ctas * s;
-        const double waves = (double)((tot + sms - 1) / (sms > 0 ? sms : 1));
-        const double t = waves * ((double)bps + 1.0);
+        const double t = (double)((tot + sms - 1) / sms) * ((double)bps + 1.0);
         if (t < best_t * 0.999) {
             best_t = t;
             best = s;
         }
     }
-    const int bps = (nblk + best - 1) / best;
+    int bps = (nblk + best - 1) / best;
     p->nsplit = best;
     p->keys_per_split = bps * ATTN_GPU_KEY_TILE;
+    if (best > 1 || !tc || p->causal || ctas <= sms) return;
+    const int L = ctas % sms;
+    if (L == 0 || 2 * L > sms) return;
+    const int ur = ts_tc_unit_rows(p);
+    const int tiles = ctas / p->Hkv;
+    const int u0 = ctas - L;
+    const long long rows_per_kv = (long long)(p->Hq / p->Hkv) * p->Sq;
+    const long long row_base = (long long)(u0 / tiles) * rows_per_kv + (long long)(u0 % tiles) * ur;
+    int s = sms / L;
+    if (s > nblk / 2) s = nblk / 2;
+    while (s >= 2 && (rows - row_base) * s > ATTN_PARTIAL_ROWS) --s;
+    if (s < 2) return;
+    bps = (nblk + s - 1) / s;
+    p->nsplit = (nblk + bps - 1) / bps;
+    p->keys_per_split = bps * ATTN_GPU_KEY_TILE;
+    p->n_direct = u0;
+    p->row_base = (int)row_base;
 }
 
 static int ts_validate(const void *Q, const void *K, const void *V, int Hq, int Hkv, int Sq, int Sk, int D,
@@ -153,8 +177,7 @@ static int ts_run(fa_problem *p, void *scratch, void *stream) {
     ts_scratch s;
     ts_scratch_layout(scratch, p->D, &s);
     p->status = s.status;
-    const int ctas = ts_tc_supported(p) ? ts_tc_ctas_per_split(p) : (int)(((long long)p->Hq * p->Sq + 7) / 8);
-    ts_plan_splits(p, ctas);
+    ts_plan(p);
     if (p->nsplit > 1) {
         p->part_m = s.m;
         p->part_l = s.l;

@@ -15,7 +15,7 @@
 #include "attn_flash.h"
 #include "fa_launch.h"
 
-extern "C" int ts_launch_tc(const fa_problem *P, void *stream, int partial);
+extern "C" int ts_launch_tc(const fa_problem *P, void *stream);
 
 static std::atomic<unsigned long long> g_kernel_launches{0};
 
@@ -217,13 +217,16 @@ static int launch_simt(const fa_problem *P, void *stream, int partial) {
 }
 
 extern "C" int ts_launch_attention(const fa_problem *P, void *stream) {
-    const int partial = (P->nsplit > 1 || P->write_partials) ? 1 : 0;
-    int rc = ts_tc_supported(P) ? ts_launch_tc(P, stream, partial) : launch_simt(P, stream, partial);
+    const bool tc = ts_tc_supported(P) != 0;
+    int rc = tc ? ts_launch_tc(P, stream) : launch_simt(P, stream, (P->nsplit > 1 || P->write_partials) ? 1 : 0);
     if (rc != ATTN_OK || P->nsplit <= 1) return rc;
+    // merge the key pieces of the split rows [base, Hq*Sq) (all rows on the general path)
     const int rows = P->Hq * P->Sq;
-    return ts_launch_combine(P->part_m, P->part_l, P->part_acc, P->nsplit, rows, P->D,
-                             P->write_partials ? P->out_acc : P->O, P->write_partials ? P->out_m : nullptr,
-                             P->write_partials ? P->out_l : nullptr, stream);
+    const int base = tc ? P->row_base : 0;
+    float *out = (P->write_partials ? P->out_acc : P->O) + (size_t)base * P->D;
+    return ts_launch_combine(P->part_m, P->part_l, P->part_acc, P->nsplit, rows - base, P->D, out,
+                             P->write_partials ? P->out_m + base : nullptr,
+                             P->write_partials ? P->out_l + base : nullptr, stream);
 }
 
 extern "C" int ts_clear_status(int *status, void *stream) {

@@ -53,14 +53,18 @@ constexpr float kRescaleLog2 = 8.0f;  // lazy max update threshold, in log2 unit
 constexpr int kSmemBudget = 200 * 1024;
 
 struct TcParams {
-    float *O;
-    float *part_m, *part_l, *part_acc;
+    float *O;                          // normalised output (global rows)
+    float *out_m, *out_l, *out_acc;    // caller partials (global rows) when write_partials
+    float *part_m, *part_l, *part_acc; // key-piece partials [piece][row - row_base]
     int *status;
     int rows_per_kv;  // group * Sq
     int total_rows;   // Hq * Sq
     int Sq, Sk, Sk_total, k_begin;
-    int D, causal;
-    int keys_per_split;
+    int D, causal, Hkv, tiles_per_kv;
+    int n_direct;        // units [0, n_direct) run whole; the rest as `pieces` key pieces
+    int pieces, keys_per_piece;
+    int row_base, part_rows;  // split units cover global rows [row_base, row_base + part_rows)
+    int write_partials;
     float scale_log2;
 };
 
@@ -94,7 +98,9 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int *s
     }
 }
 
-template <int DP, int NQT, bool VT, bool PARTIAL>
+// GENERAL=false: every CTA runs a whole unit and writes normalised O (plain prefill/decode
+// without splits); GENERAL=true adds key pieces and caller-partial output.
+template <int DP, int NQT, bool VT, bool GENERAL>
 __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const TcParams p) {
@@ -124,12 +130,33 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     const int lane = threadIdx.x & 31;
 
     // ---------------- work item
-    const int kv = blockIdx.y;
-    const int split = blockIdx.z;
-    const int tile_idx = p.causal ? (int)(gridDim.x - 1 - blockIdx.x) : (int)blockIdx.x;
-    const int row0 = tile_idx * kBM * NQT;
-    const int kb0 = split * p.keys_per_split;            // local key range [kb0, kb1)
-    const int kb1 = min(p.Sk, kb0 + p.keys_per_split);
+    // Which unit (row tile of one kv head) and which key piece this CTA runs.
+    // !GENERAL: 2-D grid, one CTA per unit: (tiles, Hkv), or with causal masking (Hkv, tiles)
+    //   walked from the highest row tile down, so the longest units start first.
+    // GENERAL: 1-D grid over kv-major units; units below n_direct run whole, each later unit
+    //   runs as `pieces` key pieces.
+    int kv, tile, piece = -1;
+    if (!GENERAL) {
+        if (p.causal) {
+            kv = blockIdx.x;
+            tile = p.tiles_per_kv - 1 - (int)blockIdx.y;
+        } else {
+            tile = blockIdx.x;
+            kv = blockIdx.y;
+        }
+    } else {
+        int u = blockIdx.x;
+        if (u >= p.n_direct) {
+            const int q = u - p.n_direct;
+            u = p.n_direct + q / p.pieces;
+            piece = q % p.pieces;
+        }
+        kv = u / p.tiles_per_kv;
+        tile = u % p.tiles_per_kv;
+    }
+    const int row0 = tile * kBM * NQT;
+    const int kb0 = piece < 0 ? 0 : piece * p.keys_per_piece;  // local key range [kb0, kb1)
+    const int kb1 = piece < 0 ? p.Sk : min(p.Sk, kb0 + p.keys_per_piece);
     int kend = kb1;
     if (p.causal) {
         const int rlast = min(row0 + kBM * NQT, p.rows_per_kv) - 1;
@@ -440,13 +467,16 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             const size_t grow = (size_t)kv * p.rows_per_kv + prow;  // row of [Hq*Sq]
             float *dst;
             float mult;
-            if (PARTIAL) {
-                const size_t prow_g = (size_t)split * p.total_rows + grow;
+            if (GENERAL && (piece >= 0 || p.write_partials)) {
+                // (m, l, unnormalised acc): a key piece's slot, or the caller's partial row
+                const size_t slot = piece >= 0 ? (size_t)piece * p.part_rows + (grow - p.row_base) : grow;
+                float *pm = piece >= 0 ? p.part_m : p.out_m;
+                float *pl = piece >= 0 ? p.part_l : p.out_l;
                 if (valid) {
-                    p.part_m[prow_g] = (m == -INFINITY) ? -INFINITY : __fmul_rn(m, sl2);
-                    p.part_l[prow_g] = l;
+                    pm[slot] = (m == -INFINITY) ? -INFINITY : __fmul_rn(m, sl2);
+                    pl[slot] = l;
                 }
-                dst = p.part_acc + prow_g * D;
+                dst = (piece >= 0 ? p.part_acc : p.out_acc) + slot * D;
                 mult = 1.f;
             } else {
                 dst = p.O + grow * D;
@@ -513,10 +543,11 @@ static bool make_map_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t 
     return r == CUDA_SUCCESS;
 }
 
-template <int DP, int NQT, bool VT, bool PARTIAL>
-static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
+template <int DP, int NQT, bool VT, bool GENERAL>
+static int launch_tc_inst(cudaStream_t st, const CUtensorMap &tmQ, const CUtensorMap &tmK, const CUtensorMap &tmV,
+                          const TcParams &prm, dim3 grid) {
     using C = TcConfig<DP, NQT>;
-    auto kern = fa_tc_kernel<DP, NQT, VT, PARTIAL>;
+    auto kern = fa_tc_kernel<DP, NQT, VT, GENERAL>;
     static int attr_done[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return ATTN_ERR_CUDA;
@@ -525,6 +556,14 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
             return ATTN_ERR_CUDA;
         attr_done[dev] = 1;
     }
+    kern<<<grid, C::THREADS, C::SMEM, st>>>(tmQ, tmK, tmV, prm);
+    if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
+    ts_count_launch();
+    return ATTN_OK;
+}
+
+template <int DP, int NQT, bool VT>
+static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     const int group = P->Hq / P->Hkv;
     const uint64_t rows = (uint64_t)group * P->Sq;
     const uint64_t D = (uint64_t)P->D;
@@ -539,6 +578,9 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     }
     TcParams prm;
     prm.O = P->O;
+    prm.out_m = P->out_m;
+    prm.out_l = P->out_l;
+    prm.out_acc = P->out_acc;
     prm.part_m = P->part_m;
     prm.part_l = P->part_l;
     prm.part_acc = P->part_acc;
@@ -551,13 +593,22 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     prm.k_begin = P->k_begin;
     prm.D = P->D;
     prm.causal = P->causal;
-    prm.keys_per_split = P->keys_per_split;
+    prm.Hkv = P->Hkv;
+    prm.tiles_per_kv = tiles_per_kv;
+    const int units = tiles_per_kv * P->Hkv;
+    prm.n_direct = P->nsplit > 1 ? P->n_direct : units;
+    prm.pieces = P->nsplit > 1 ? P->nsplit : 1;
+    prm.keys_per_piece = P->keys_per_split;
+    prm.row_base = P->row_base;
+    prm.part_rows = P->Hq * P->Sq - P->row_base;
+    prm.write_partials = P->write_partials;
     prm.scale_log2 = P->scale_log2;
-    dim3 grid(tiles_per_kv, P->Hkv, P->nsplit);
-    kern<<<grid, C::THREADS, C::SMEM, st>>>(tmQ, tmK, tmV, prm);
-    if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
-    ts_count_launch();
-    return ATTN_OK;
+    if (prm.n_direct == units && !prm.write_partials) {
+        const dim3 grid = prm.causal ? dim3(P->Hkv, tiles_per_kv) : dim3(tiles_per_kv, P->Hkv);
+        return launch_tc_inst<DP, NQT, VT, false>(st, tmQ, tmK, tmV, prm, grid);
+    }
+    return launch_tc_inst<DP, NQT, VT, true>(st, tmQ, tmK, tmV, prm,
+                                             dim3(prm.n_direct + (units - prm.n_direct) * prm.pieces));
 }
 
 static int nqt_for(const fa_problem *P) {
@@ -577,6 +628,8 @@ extern "C" int ts_tc_supported(const fa_problem *P) {
     return 1;
 }
 
+extern "C" int ts_tc_unit_rows(const fa_problem *P) { return ts::kBM * ts::nqt_for(P); }
+
 extern "C" int ts_tc_ctas_per_split(const fa_problem *P) {
     const long long rows = (long long)(P->Hq / P->Hkv) * P->Sq;
     const int nqt = ts::nqt_for(P);
@@ -584,7 +637,7 @@ extern "C" int ts_tc_ctas_per_split(const fa_problem *P) {
     return (int)(tiles * P->Hkv);
 }
 
-extern "C" int ts_launch_tc(const fa_problem *P, void *stream, int partial) {
+extern "C" int ts_launch_tc(const fa_problem *P, void *stream) {
     using namespace ts;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const long long rows = (long long)(P->Hq / P->Hkv) * P->Sq;
@@ -594,10 +647,7 @@ extern "C" int ts_launch_tc(const fa_problem *P, void *stream, int partial) {
     const bool vt = P->v_prepacked != 0;
 #define TS_LAUNCH(DPV, NQTV)                                                                      \
     do {                                                                                          \
-        if (vt) return partial ? launch_tc<DPV, NQTV, true, true>(P, st, tiles)                   \
-                               : launch_tc<DPV, NQTV, true, false>(P, st, tiles);                 \
-        return partial ? launch_tc<DPV, NQTV, false, true>(P, st, tiles)                          \
-                       : launch_tc<DPV, NQTV, false, false>(P, st, tiles);                        \
+        return vt ? launch_tc<DPV, NQTV, true>(P, st, tiles) : launch_tc<DPV, NQTV, false>(P, st, tiles); \
     } while (0)
     if (dp == 64) {
         if (nqt == 2) TS_LAUNCH(64, 2);

@@ -31,6 +31,14 @@ typedef struct fa_problem {
     int nsplit;                /* >1: split the key range, write partials, then combine */
     int keys_per_split;        /* multiple of the key tile */
     int write_partials;        /* 1: leave the result as (m, l, acc) partials, no combine */
+    /* Tensor-core path work plan. Units (query-row tiles of one kv head, kv-major) below
+     * n_direct run over the whole key range; units from n_direct on run as `nsplit` key pieces
+     * of keys_per_split keys each, writing partials [piece][row - row_base] (row = global row
+     * of [Hq*Sq]; the split units' rows are exactly [row_base, Hq*Sq)), merged by the combine.
+     * Decode splits every unit (n_direct = 0); a prefill whose last wave would run less than
+     * half full splits only that wave's units. */
+    int n_direct;
+    int row_base;
     float scale_log2;          /* (1/sqrt(D)) * log2(e) */
 } fa_problem;
 
@@ -41,8 +49,9 @@ int ts_cc_major(void);
 /* The tcgen05 path applies to this problem (D multiple of 8, <= 128, aligned pointers,
  * Sk multiple of 8 when V is pre-transposed). Otherwise the SIMT path runs. */
 int ts_tc_supported(const fa_problem *p);
-/* CTAs the tcgen05 path launches per split for this problem (split planning input). */
+/* Units (CTAs per split) of the tcgen05 path for this problem, and query rows per unit. */
 int ts_tc_ctas_per_split(const fa_problem *p);
+int ts_tc_unit_rows(const fa_problem *p);
 
 /* Launch the main kernel (tcgen05 or SIMT path chosen inside) plus, when nsplit > 1 and
  * !write_partials, the combine kernel. Returns 0 or a negative ATTN_ERR_* code. */
