@@ -17,7 +17,10 @@ Keys of the JSON line beyond the base contract:
                 shim) timed on this host's cores on a bounded sample of the same workload
   e2e           the same metric through the C ABI with pinned host buffers: every step copies
                 Q, K, V host->device and O device->host inside the timed region
-  decode        a secondary HBM-bound line: BASELINE config 3 (GQA decode, B=64, Sk=8192)
+  decode        a secondary HBM-bound line: BASELINE config 3 (GQA decode, B=64, Sk=8192), per GPU
+  long_decode   BASELINE config 5 decode (B=4, Hq=64, Hkv=8, Sk=131072) with the key axis split
+                over all ranks: partial attention per rank, one NCCL all-gather of the (m, l, acc)
+                partials, merge on every rank (transfer_station_b200.multigpu)
   gpu_launches  kernels the library launched inside the timed region (its own counter)
   clocks        SM clocks / throttle reasons sampled by NVML during the timed region
 
@@ -138,7 +141,8 @@ class ClockSampler:
             try:
                 mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
                 rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                self.samples.append((time.perf_counter(), mhz, rs))
+                pw = self.nv.nvmlDeviceGetPowerUsage(self.h) / 1000.0
+                self.samples.append((time.perf_counter(), mhz, rs, pw))
             except Exception:  # noqa: BLE001
                 pass
             time.sleep(0.002)
@@ -165,8 +169,9 @@ class ClockSampler:
         for s in inside:
             bits |= s[2]
         reasons = [k for k, v in self.REASONS.items() if bits & v and k != "gpu_idle"]
+        pw = sorted(s[3] for s in inside)
         return {"sm_mhz": mhz[len(mhz) // 2], "sm_max_mhz": self.max_mhz, "reasons": reasons,
-                "samples": len(inside)}
+                "power_w_median": pw[len(pw) // 2], "samples": len(inside)}
 
 
 # ------------------------------------------------------------------ CPU reference timing
@@ -406,6 +411,43 @@ def run_ours(args, w) -> None:
                        "l2": "K+V = 2 GiB per step > L2"}
         del tq, tk, tv, to
 
+    # ---------------- long-context decode, key axis split over the ranks (NCCL merge)
+    long_line = None
+    if not args.no_decode:
+        from transfer_station_b200 import multigpu
+
+        B, lHq, lHkv, lSk, lD = 4, 64, 8, 131072, 128
+        Hq5, Hkv5 = B * lHq, B * lHkv
+        k0, kl = multigpu.key_shard(lSk, world, rank)
+        g = torch.Generator(device=dev)
+        g.manual_seed(4)
+        lq = (torch.randn(Hq5 * lD, device=dev, generator=g) * 0.5).to(torch.bfloat16).view(torch.int16)
+        g.manual_seed(1000 + rank)
+        lk = (torch.randn(Hkv5 * kl * lD, device=dev, generator=g) * 0.5).to(torch.bfloat16).view(torch.int16)
+        lv = (torch.randn(Hkv5 * kl * lD, device=dev, generator=g) * 0.5).to(torch.bfloat16).view(torch.int16)
+        lo = torch.empty(Hq5 * lD, dtype=torch.float32, device=dev)
+        lsteps = max(3, min(args.steps, 100))
+        for _ in range(3):
+            multigpu.sharded_decode(lq, lk, lv, lo, Hq5, Hkv5, 1, lSk, k0, lD, 0, scratch)
+        barrier()
+        e0.record(stream)
+        for _ in range(lsteps):
+            multigpu.sharded_decode(lq, lk, lv, lo, Hq5, Hkv5, 1, lSk, k0, lD, 0, scratch)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        lms = max_over_ranks(e0.elapsed_time(e1)) / lsteps
+        rc, code = ts.attn_flash_status(scratch, stream)
+        if rc != ts.ATTN_OK:
+            raise ts.AttnError(rc, f"long decode device status {code}")
+        lby = algo_bytes(Hq5, Hkv5, 1, lSk, lD)
+        long_line = {"workload": "gqa_long_decode_b4_sk131072", "value": lby / (lms / 1e3) / 1e9, "unit": "GB/s",
+                     "per_gpu_gbs": lby / (lms / 1e3) / 1e9 / world, "ms_per_step": lms,
+                     "frac_of_measured_hbm_per_gpu": lby / (lms / 1e3) / 1e9 / world / peaks["hbm_gbs"],
+                     "bytes_per_step": lby, "steps": lsteps, "scaling": "strong (key axis split over ranks)",
+                     "merge": "one NCCL all-gather each of m, l [B*Hq] and acc [B*Hq, D] fp32, then combine"}
+        del lq, lk, lv, lo
+
     # ---------------- CPU baseline (rank 0, N=1 only)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
@@ -431,6 +473,7 @@ def run_ours(args, w) -> None:
             "gpu_launches": int(launches),
             "clocks": csum,
             "decode": decode_line,
+            "long_decode": long_line,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -1,0 +1,99 @@
+"""CPU, world_size 2 over `gloo`: the multi-GPU decomposition's host logic.
+
+The key-axis split of long-context decode (transfer_station_b200.multigpu): each rank computes
+the (m, l, acc) partials of its key shard (here with a numpy stand-in for the partial kernel,
+using the kernel's conventions: m in base-2 units of the scaled score, l and acc unnormalised),
+the partials are all-gathered with torch.distributed, and the merge (the same formula the
+combine kernel applies, restated in oracle/) must equal one-shot attention over all keys.
+Also the prefill unit split and the key-shard boundaries."""
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from transfer_station_b200 import multigpu
+
+
+def np_partial(Q, K, V, Hq, Hkv, Sq, Sk_total, k_begin, Sk_local, D, causal):
+    """(m, l, acc) of keys [k_begin, k_begin + Sk_local) for every row of [Hq*Sq]."""
+    q = oracle.bf16_to_f32(Q).reshape(Hq, Sq, D).astype(np.float64)
+    k = oracle.bf16_to_f32(K).reshape(Hkv, Sk_local, D).astype(np.float64)
+    v = oracle.bf16_to_f32(V).reshape(Hkv, Sk_local, D).astype(np.float64)
+    g = Hq // Hkv
+    c = (1.0 / np.sqrt(D)) * np.log2(np.e)
+    m = np.full(Hq * Sq, -np.inf, np.float32)
+    l = np.zeros(Hq * Sq, np.float32)
+    acc = np.zeros((Hq * Sq, D), np.float32)
+    keys = k_begin + np.arange(Sk_local)
+    for h in range(Hq):
+        s = (q[h] @ k[h // g].T) * c  # [Sq, Sk_local]
+        if causal:
+            lim = Sk_total - Sq + np.arange(Sq)
+            s = np.where(keys[None, :] <= lim[:, None], s, -np.inf)
+        mx = s.max(axis=1)
+        live = np.isfinite(mx)
+        p = np.where(live[:, None], np.exp2(s - np.where(live, mx, 0)[:, None]), 0.0)
+        r = slice(h * Sq, (h + 1) * Sq)
+        m[r] = mx
+        l[r] = p.sum(1)
+        acc[r] = p @ v[h // g]
+    return m, l, acc
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, case, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        Hq, Hkv, Sq, Sk, D, causal = case
+        Q, K, V = oracle.lcg_inputs(Hq, Hkv, Sq, Sk, D)
+        k0, kl = multigpu.key_shard(Sk, world, rank, align=64)
+        Ks = np.ascontiguousarray(K.reshape(Hkv, Sk, D)[:, k0:k0 + kl]).reshape(-1)
+        Vs = np.ascontiguousarray(V.reshape(Hkv, Sk, D)[:, k0:k0 + kl]).reshape(-1)
+        m, l, acc = np_partial(Q, Ks, Vs, Hq, Hkv, Sq, Sk, k0, kl, D, causal)
+        all_m, all_l, all_acc = multigpu.gather_partials(torch.from_numpy(m), torch.from_numpy(l),
+                                                         torch.from_numpy(acc))
+        O = oracle.combine(all_m.numpy(), all_l.numpy(), all_acc.numpy(), world, Hq * Sq, D)
+        if rank == 0:
+            np.save(out_path, O)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", [(8, 2, 1, 1000, 64, 0), (4, 2, 40, 300, 32, 1)])
+def test_key_sharded_merge_two_ranks(tmp_path, case):
+    world = 2
+    out = tmp_path / "o.npy"
+    mp.spawn(_worker, args=(world, _free_port(), case, str(out)), nprocs=world, join=True)
+    Hq, Hkv, Sq, Sk, D, causal = case
+    Q, K, V = oracle.lcg_inputs(Hq, Hkv, Sq, Sk, D)
+    rows = np.arange(Sq, dtype=np.int32)
+    ref = oracle.attn_ref(Q, K, V, Hq, Hkv, Sq, Sk, D, causal, rows)
+    c = oracle.cmp_rows(ref, np.load(out), Hq, Sq, D, rows)
+    assert c["nbad"] == 0 and c["mad"] < 1e-5, c  # no bf16 P here: exact up to fp32 sums
+
+
+def test_unit_and_key_shards_partition():
+    for n, world in [(8, 8), (32, 8), (7, 4), (3, 8), (1024, 3)]:
+        spans = [multigpu.unit_shard(n, world, r) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == n
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+        assert max(e - s for s, e in spans) - min(e - s for s, e in spans) <= 1
+    for Sk, world in [(131072, 8), (131072, 3), (1000, 4), (100, 8)]:
+        sh = [multigpu.key_shard(Sk, world, r) for r in range(world)]
+        assert sum(k for _, k in sh) == Sk
+        assert all(b % 128 == 0 or b == Sk for b, _ in sh)
+        assert all(sh[r][0] + sh[r][1] == sh[r + 1][0] for r in range(world - 1))

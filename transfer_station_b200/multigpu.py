@@ -1,0 +1,87 @@
+"""Multi-GPU partitioning of the attention path (one process per GPU, torch.distributed).
+
+Two decompositions, as the work shards (none of them exists in flash.c, which is one call on one
+core):
+
+* Prefill shards by (batch x kv-head group): the units are independent -- every query head of
+  a group reads only its kv head's K/V -- so each rank runs attn_flash on whole kv groups and
+  writes its own slice of O. No collective.
+
+* Long-context decode with few kv heads shards the KEY axis: rank r holds keys
+  [k_begin, k_begin + Sk_local) of every kv head, runs attn_flash_partial_stream on them
+  (masking by global key position), the per-row partials (m, l, acc) -- a few hundred KB --
+  are all-gathered over NVLink with NCCL, and every rank merges them with
+  attn_flash_combine_stream into the full output. This is the key loop of flash.c:798 split
+  across GPUs, with the online-softmax merge of flash.c:535-576 applied across shards.
+
+The exchange uses only torch.distributed collectives, so the same code runs with the `gloo`
+backend on CPU tensors (the tests do that with a CPU stand-in for the partial kernel).
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+import transfer_station_b200 as ts
+
+
+def unit_shard(n_units: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous share [start, end) of n_units independent units for `rank` (the first
+    n_units % world ranks take one more)."""
+    base, extra = divmod(n_units, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def key_shard(Sk: int, world: int, rank: int, align: int = ts.ATTN_GPU_KEY_TILE) -> tuple[int, int]:
+    """Key range (k_begin, k_len) of `rank` when Sk keys are split over `world` ranks. Shard
+    boundaries fall on multiples of `align` (the kernel's key tile) so no tile straddles two
+    ranks; the last rank takes the remainder. A rank may get an empty range when Sk is small."""
+    blocks = -(-Sk // align)
+    b0, b1 = unit_shard(blocks, world, rank)
+    k0 = min(Sk, b0 * align)
+    k1 = min(Sk, b1 * align)
+    return k0, k1 - k0
+
+
+def gather_partials(m: torch.Tensor, l: torch.Tensor, acc: torch.Tensor, group=None):
+    """All-gather the per-row partials of every rank: m, l [rows] and acc [rows, D] become
+    [world, rows] and [world, rows, D] (one NCCL all-gather each on GPU tensors)."""
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
+        return [t.contiguous().unsqueeze(0) for t in (m, l, acc)]  # one rank: nothing to exchange
+    world = dist.get_world_size(group)
+    outs = []
+    for t in (m, l, acc):
+        t = t.contiguous()
+        o = torch.empty(world * t.numel(), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(o, t.reshape(-1), group=group)
+        outs.append(o.view((world,) + tuple(t.shape)))
+    return outs
+
+
+def sharded_decode(q, k_shard, v_shard, O, Hq: int, Hkv: int, Sq: int, Sk_total: int, k_begin: int, D: int,
+                   causal: int, scratch, bk: int = ts.ATTN_BK_DEFAULT, group=None, stream=None):
+    """Attention over a key axis split across the ranks of `group`. Every rank passes its own
+    K/V shard ([Hkv][Sk_local][D], keys k_begin.. of the global axis) and the full Q; every rank
+    receives the full O [Hq*Sq*D] (fp32). Raises AttnError on a library error."""
+    rows = Hq * Sq
+    Sk_local = k_shard.numel() // (Hkv * D)
+    dev = q.device
+    m = torch.empty(rows, dtype=torch.float32, device=dev)
+    l = torch.empty(rows, dtype=torch.float32, device=dev)
+    acc = torch.empty(rows, D, dtype=torch.float32, device=dev)
+    if Sk_local > 0:
+        rc = ts.attn_flash_partial_stream(q, k_shard, v_shard, m, l, acc, Hq, Hkv, Sq, Sk_local, Sk_total, k_begin,
+                                          D, causal, bk, scratch, 0, stream)
+        if rc != ts.ATTN_OK:
+            raise ts.AttnError(rc, "attn_flash_partial_stream")
+    else:  # an empty shard contributes nothing: m = -inf, l = 0
+        m.fill_(float("-inf"))
+        l.zero_()
+        acc.zero_()
+    all_m, all_l, all_acc = gather_partials(m, l, acc, group)
+    world = all_m.shape[0]
+    rc = ts.attn_flash_combine_stream(all_m, all_l, all_acc, world, rows, D, O, stream)
+    if rc != ts.ATTN_OK:
+        raise ts.AttnError(rc, "attn_flash_combine_stream")
+    return O
