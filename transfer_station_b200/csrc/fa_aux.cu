@@ -119,8 +119,12 @@ __global__ void __launch_bounds__(256) fa_simt_kernel(const SimtParams p) {
     }
 }
 
-// One warp per row: O[r] = sum_s 2^(m_s - m*) acc_s[r] / sum_s 2^(m_s - m*) l_s[r].
-// With out_m != nullptr the merged partial (m*, L, unnormalised acc) is written instead.
+// One warp per row: O[r] = sum_s 2^(m_s - m*) acc_s[r] / sum_s 2^(m_s - m*) l_s[r] (zero row
+// when every l_s is 0). With out_m != nullptr the merged partial (m*, L, unnormalised acc) is
+// written instead. The lanes read the parts' m and l in parallel and reduce them with shuffles;
+// then lane i owns columns 4i..4i+3 (VEC, D % 4 == 0) or column i of every 32 (scalar), and the
+// loads of all parts are independent, so a row's reads are in flight together.
+template <bool VEC>
 __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict__ m, const float *__restrict__ l,
                                                          const float *__restrict__ acc, int nparts, int rows, int D,
                                                          float *__restrict__ out, float *__restrict__ out_m,
@@ -129,20 +133,43 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict
     const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= rows) return;
     float mx = -INFINITY;
-    for (int s = 0; s < nparts; ++s) mx = fmaxf(mx, m[(size_t)s * rows + r]);
+    for (int s = lane; s < nparts; s += 32) mx = fmaxf(mx, m[(size_t)s * rows + r]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float L = 0.f;
-    for (int s = 0; s < nparts; ++s) {
+    for (int s = lane; s < nparts; s += 32) {
         const float ms = m[(size_t)s * rows + r];
         if (ms != -INFINITY) L = fmaf(ex2f(ms - mx), l[(size_t)s * rows + r], L);
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
     const float inv = out_m ? 1.f : ((L > 0.f) ? 1.f / L : 0.f);
-    for (int c = lane; c < D; c += 32) {
-        float a = 0.f;
-        for (int s = 0; s < nparts; ++s) {
-            const float ms = m[(size_t)s * rows + r];
-            if (ms != -INFINITY) a = fmaf(ex2f(ms - mx), acc[((size_t)s * rows + r) * D + c], a);
+    if (VEC) {
+        for (int c = 4 * lane; c < D; c += 128) {
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+            for (int s = 0; s < nparts; ++s) {
+                const float ms = m[(size_t)s * rows + r];
+                const float w = (ms != -INFINITY) ? ex2f(ms - mx) : 0.f;
+                const float4 x = *reinterpret_cast<const float4 *>(acc + ((size_t)s * rows + r) * D + c);
+                a.x = fmaf(w, x.x, a.x);
+                a.y = fmaf(w, x.y, a.y);
+                a.z = fmaf(w, x.z, a.z);
+                a.w = fmaf(w, x.w, a.w);
+            }
+            *reinterpret_cast<float4 *>(out + (size_t)r * D + c) = make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
         }
-        out[(size_t)r * D + c] = a * inv;
+    } else {
+        for (int c = lane; c < D; c += 32) {
+            float a = 0.f;
+#pragma unroll 4
+            for (int s = 0; s < nparts; ++s) {
+                const float ms = m[(size_t)s * rows + r];
+                const float w = (ms != -INFINITY) ? ex2f(ms - mx) : 0.f;
+                a = fmaf(w, acc[((size_t)s * rows + r) * D + c], a);
+            }
+            out[(size_t)r * D + c] = a * inv;
+        }
     }
     if (out_m && lane == 0) {
         out_m[r] = mx;
@@ -179,8 +206,13 @@ extern "C" int ts_launch_combine(const float *m, const float *l, const float *ac
     if (rows <= 0) return ATTN_OK;
     const int warps = 8;
     dim3 grid((rows + warps - 1) / warps);
-    ts::fa_combine_kernel<<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows, D, O,
-                                                                                      out_m, out_l);
+    const bool vec = (D % 4 == 0) && ((((uintptr_t)acc) | ((uintptr_t)O)) & 15u) == 0;
+    if (vec)
+        ts::fa_combine_kernel<true><<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows,
+                                                                                               D, O, out_m, out_l);
+    else
+        ts::fa_combine_kernel<false><<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows,
+                                                                                                D, O, out_m, out_l);
     if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
     ts_count_launch();
     return ATTN_OK;
