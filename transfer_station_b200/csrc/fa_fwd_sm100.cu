@@ -347,62 +347,42 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
         const float sl2 = p.scale_log2;
 
         float m = -INFINITY, l = 0.f;
+        float ms = 0.f;  // m * scale_log2, rounded once (0 while m is -inf)
         bool ok = true;
+        const float2 c2 = make_float2(sl2, sl2);
         for (int j = 0; j < nblk; ++j) {
             ok = mbar_wait(s_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutS);
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
-            uint32_t sr[128];
-            tmem_ld128(tS, sr);
             const long long key0 = kb0 + (long long)j * kBN;
             const long long nv = lastkey - key0 + 1;
             // `full`: every row of this warp sees every key of the block (no tail, no causal
-            // cut); then the warp takes the fast path below, else the exact masked path. The
-            // choice must be warp-uniform: both paths issue warp-collective tcgen05.st.
+            // cut). The choice must be warp-uniform: every path issues warp-collective tcgen05.st.
             const bool full = __all_sync(0xffffffffu, nv >= kBN);
-            float mb;
-            if (full) {
-                float mx[8];
-#pragma unroll
-                for (int k = 0; k < 8; ++k) mx[k] = fmax3(u2f(sr[k]), u2f(sr[8 + k]), u2f(sr[16 + k]));
-#pragma unroll
-                for (int c = 24; c < 128; c += 16)
-#pragma unroll
-                    for (int k = 0; k < 8; ++k) mx[k] = fmax3(mx[k], u2f(sr[c + k]), u2f(sr[c + 8 + k]));
-                mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
-            } else {
-                const int nvalid = nv < 0 ? 0 : (int)nv;
-#pragma unroll
-                for (int c = 0; c < 128; ++c)
-                    if (c >= nvalid) sr[c] = f2u(-INFINITY);
-                float mx0 = u2f(sr[0]), mx1 = u2f(sr[1]), mx2 = u2f(sr[2]), mx3 = u2f(sr[3]);
-#pragma unroll
-                for (int c = 4; c < 128; c += 4) {
-                    mx0 = fmaxf(mx0, u2f(sr[c]));
-                    mx1 = fmaxf(mx1, u2f(sr[c + 1]));
-                    mx2 = fmaxf(mx2, u2f(sr[c + 2]));
-                    mx3 = fmaxf(mx3, u2f(sr[c + 3]));
-                }
-                mb = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
-            }
-            float m_new = m;
-            if (mb > m && (m == -INFINITY || (mb - m) * sl2 > kRescaleLog2)) m_new = mb;
-            const float alpha = (m_new == m) ? 1.f : ((m == -INFINITY) ? 0.f : ex2((m - m_new) * sl2));
-            const float ms = (m_new == -INFINITY) ? 0.f : __fmul_rn(m_new, sl2);
+            // `spec`: a full block of a warp whose rows all have a running max. P is computed
+            // against that max while the block's own max is tracked alongside, so the
+            // exponentials do not wait for a max pass over all 128 columns first. Only when some
+            // row's block max exceeds its running max by more than kRescaleLog2 (in log2 units)
+            // does the warp redo the block exactly below (rare: the first block sets a max that
+            // later blocks seldom exceed by that much).
+            const bool spec = full && __all_sync(0xffffffffu, m != -INFINITY);
+            uint32_t sr[128];
             float rs0 = 0.f, rs1 = 0.f;
-            if (full) {
-                // P = 2^(s*c - m*c) by one packed FMA per pair; 3 of every 8 pairs take the
-                // polynomial exp2 on the FMA pipe, the rest the MUFU unit, so both run at once.
-                const float2 c2 = make_float2(sl2, sl2), nms2 = make_float2(-ms, -ms);
+            bool redo = true;
+            if (spec) {
+                const float2 nms2 = make_float2(-ms, -ms);
                 float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+                float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                tmem_ld32p(tS, sr);
 #pragma unroll
                 for (int cc = 0; cc < 4; ++cc) {
                     uint32_t pk[16];
 #pragma unroll
                     for (int u = 0; u < 16; ++u) {
-                        const float2 x = __ffma2_rn(make_float2(u2f(sr[32 * cc + 2 * u]), u2f(sr[32 * cc + 2 * u + 1])),
-                                                    c2, nms2);
+                        const float s0 = u2f(sr[32 * cc + 2 * u]), s1 = u2f(sr[32 * cc + 2 * u + 1]);
+                        mx[u & 3] = fmax3(mx[u & 3], s0, s1);
+                        const float2 x = __ffma2_rn(make_float2(s0, s1), c2, nms2);
                         float2 pr;
                         if ((u & 7) < 3) {
                             pr = exp2_fma2(x);
@@ -416,38 +396,109 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                             acc0 = __fadd2_rn(acc0, pr);
                         pk[u] = pack_bf16x2(pr.x, pr.y);
                     }
+                    // the next 32 score columns (load and wait in one statement) before this
+                    // chunk's P goes to columns [16cc, 16cc+16), which were already read
+                    if (cc < 3) tmem_ld32p(tS + 32 * (cc + 1), sr + 32 * (cc + 1));
                     tmem_st16(tS + cc * 16, pk);
                 }
                 rs0 = acc0.x + acc1.x;
                 rs1 = acc0.y + acc1.y;
+                const float mb = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+                redo = __any_sync(0xffffffffu, mb > m && (mb - m) * sl2 > kRescaleLog2);
+                if (redo) tmem_wait_st();  // the speculative P stores land before the exact ones
             } else {
-#pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    uint32_t pk[16];
-#pragma unroll
-                    for (int u = 0; u < 16; ++u) {
-                        // Rounded multiply, then subtract (never fused): the row's max element
-                        // gives exactly 2^0 = 1, as exp(S - m) does in flash.c:566.
-                        const float p0 = ex2(__fsub_rn(__fmul_rn(u2f(sr[32 * cc + 2 * u]), sl2), ms));
-                        const float p1 = ex2(__fsub_rn(__fmul_rn(u2f(sr[32 * cc + 2 * u + 1]), sl2), ms));
-                        rs0 += p0;
-                        rs1 += p1;
-                        pk[u] = pack_bf16x2(p0, p1);
-                    }
-                    tmem_st16(tS + cc * 16, pk);
-                }
+                tmem_ld128(tS, sr);
             }
-            l = l * alpha + (rs0 + rs1);
-            m = m_new;
-            // O_t holds P V through block j-1 (complete: S_t(j) was committed after it).
-            if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+            if (!redo) {
+                l += rs0 + rs1;
+            } else {
+                float mb;
+                if (full) {
+                    float mx[8];
 #pragma unroll
-                for (int cc = 0; cc < DP / 32; ++cc) {
-                    uint32_t o[32];
-                    tmem_ld32(tO + cc * 32, o);
+                    for (int k = 0; k < 8; ++k) mx[k] = fmax3(u2f(sr[k]), u2f(sr[8 + k]), u2f(sr[16 + k]));
 #pragma unroll
-                    for (int u = 0; u < 32; ++u) o[u] = f2u(u2f(o[u]) * alpha);
-                    tmem_st32(tO + cc * 32, o);
+                    for (int c = 24; c < 128; c += 16)
+#pragma unroll
+                        for (int k = 0; k < 8; ++k) mx[k] = fmax3(mx[k], u2f(sr[c + k]), u2f(sr[c + 8 + k]));
+                    mb = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(fmax3(mx[3], mx[4], mx[5]), mx[6], mx[7]));
+                } else {
+                    const int nvalid = nv < 0 ? 0 : (int)nv;
+#pragma unroll
+                    for (int c = 0; c < 128; ++c)
+                        if (c >= nvalid) sr[c] = f2u(-INFINITY);
+                    float mx0 = u2f(sr[0]), mx1 = u2f(sr[1]), mx2 = u2f(sr[2]), mx3 = u2f(sr[3]);
+#pragma unroll
+                    for (int c = 4; c < 128; c += 4) {
+                        mx0 = fmaxf(mx0, u2f(sr[c]));
+                        mx1 = fmaxf(mx1, u2f(sr[c + 1]));
+                        mx2 = fmaxf(mx2, u2f(sr[c + 2]));
+                        mx3 = fmaxf(mx3, u2f(sr[c + 3]));
+                    }
+                    mb = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3));
+                }
+                float m_new = m;
+                if (mb > m && (m == -INFINITY || (mb - m) * sl2 > kRescaleLog2)) m_new = mb;
+                const float alpha = (m_new == m) ? 1.f : ((m == -INFINITY) ? 0.f : ex2((m - m_new) * sl2));
+                ms = (m_new == -INFINITY) ? 0.f : __fmul_rn(m_new, sl2);
+                if (full) {
+                    // P = 2^(s*c - m*c) by one packed FMA per pair; 3 of every 8 pairs take the
+                    // polynomial exp2 on the FMA pipe, the rest the MUFU unit, so both run at once.
+                    const float2 nms2 = make_float2(-ms, -ms);
+                    float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) {
+                            const float2 x = __ffma2_rn(
+                                make_float2(u2f(sr[32 * cc + 2 * u]), u2f(sr[32 * cc + 2 * u + 1])), c2, nms2);
+                            float2 pr;
+                            if ((u & 7) < 3) {
+                                pr = exp2_fma2(x);
+                            } else {
+                                pr.x = ex2(x.x);
+                                pr.y = ex2(x.y);
+                            }
+                            if (u & 1)
+                                acc1 = __fadd2_rn(acc1, pr);
+                            else
+                                acc0 = __fadd2_rn(acc0, pr);
+                            pk[u] = pack_bf16x2(pr.x, pr.y);
+                        }
+                        tmem_st16(tS + cc * 16, pk);
+                    }
+                    rs0 = acc0.x + acc1.x;
+                    rs1 = acc0.y + acc1.y;
+                } else {
+#pragma unroll
+                    for (int cc = 0; cc < 4; ++cc) {
+                        uint32_t pk[16];
+#pragma unroll
+                        for (int u = 0; u < 16; ++u) {
+                            // Rounded multiply, then subtract (never fused): the row's max element
+                            // gives exactly 2^0 = 1, as exp(S - m) does in flash.c:566.
+                            const float p0 = ex2(__fsub_rn(__fmul_rn(u2f(sr[32 * cc + 2 * u]), sl2), ms));
+                            const float p1 = ex2(__fsub_rn(__fmul_rn(u2f(sr[32 * cc + 2 * u + 1]), sl2), ms));
+                            rs0 += p0;
+                            rs1 += p1;
+                            pk[u] = pack_bf16x2(p0, p1);
+                        }
+                        tmem_st16(tS + cc * 16, pk);
+                    }
+                }
+                l = l * alpha + (rs0 + rs1);
+                m = m_new;
+                // O_t holds P V through block j-1 (complete: S_t(j) was committed after it).
+                if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+                    for (int cc = 0; cc < DP / 32; ++cc) {
+                        uint32_t o[32];
+                        tmem_ld32(tO + cc * 32, o);
+#pragma unroll
+                        for (int u = 0; u < 32; ++u) o[u] = f2u(u2f(o[u]) * alpha);
+                        tmem_st32(tO + cc * 32, o);
+                    }
                 }
             }
             tmem_wait_st();

@@ -181,6 +181,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         : "memory");
 }
 
+// Same as tmem_ld32 for a 32-register slice of a larger array.
+__device__ __forceinline__ void tmem_ld32p(uint32_t taddr, uint32_t *r) {
+    tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
+}
+
 // Two 32-column loads in flight, one wait: columns [col, col+32) and [col2, col2+32).
 __device__ __forceinline__ void tmem_ld32x2(uint32_t taddr, uint32_t taddr2, uint32_t (&r)[32],
                                             uint32_t (&q)[32]) {
