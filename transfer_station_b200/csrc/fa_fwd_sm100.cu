@@ -275,8 +275,8 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                     umma_ts(d_tmem, a_tmem + ks * 8, bdesc, idesc_pv, (accumulate || ks > 0) ? 1u : 0u);
                 }
             };
-            bool ok = mbar_wait(q_full, 0, abort_flag, p.status, kDevErrTimeoutQ) &&
-                      mbar_wait(kv_full(0), 0, abort_flag, p.status, kDevErrTimeoutKV);
+            bool ok = mbar_wait_fast(q_full, 0, abort_flag, p.status, kDevErrTimeoutQ) &&
+                      mbar_wait_fast(kv_full(0), 0, abort_flag, p.status, kDevErrTimeoutKV);
             if (ok) {
                 tc_fence_after();
 #pragma unroll
@@ -292,8 +292,8 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 const bool more = j + 1 < nblk;
 #pragma unroll
                 for (int t = 0; t < NQT; ++t) {
-                    if (!mbar_wait(p_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutP)) { ok = false; break; }
-                    if (t == 0 && !mbar_wait(kv_full(sV), (iV / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                    if (!mbar_wait_fast(p_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutP)) { ok = false; break; }
+                    if (t == 0 && !mbar_wait_fast(kv_full(sV), (iV / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
                         ok = false;
                         break;
                     }
@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                     issue_pv(t, sV, j > 0);
                     if (more) {
                         if (t == 0) {
-                            if (!mbar_wait(kv_full(sK), (iK / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                            if (!mbar_wait_fast(kv_full(sK), (iK / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
                                 ok = false;
                                 break;
                             }
