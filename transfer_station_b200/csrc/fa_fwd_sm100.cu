@@ -374,17 +374,21 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 const float2 nms2 = make_float2(-ms, -ms);
                 float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
                 float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-                tmem_ld32p(tS, sr);
+                // 16 score columns at a time: each load (and its wait) is issued right before
+                // the previous chunk's P store, and the chunk boundaries keep the compiler's
+                // schedule chunk by chunk (one upfront 128-column load measured 13% slower).
+                // 2 of every 8 pairs take the polynomial exp2 on the FMA pipe, the rest MUFU.
+                tmem_ld16p(tS, sr);
 #pragma unroll
-                for (int cc = 0; cc < 4; ++cc) {
-                    uint32_t pk[16];
+                for (int cc = 0; cc < 8; ++cc) {
+                    uint32_t pk[8];
 #pragma unroll
-                    for (int u = 0; u < 16; ++u) {
-                        const float s0 = u2f(sr[32 * cc + 2 * u]), s1 = u2f(sr[32 * cc + 2 * u + 1]);
+                    for (int u = 0; u < 8; ++u) {
+                        const float s0 = u2f(sr[16 * cc + 2 * u]), s1 = u2f(sr[16 * cc + 2 * u + 1]);
                         mx[u & 3] = fmax3(mx[u & 3], s0, s1);
                         const float2 x = __ffma2_rn(make_float2(s0, s1), c2, nms2);
                         float2 pr;
-                        if ((u & 7) < 3) {
+                        if (u < 2) {
                             pr = exp2_fma2(x);
                         } else {
                             pr.x = ex2(x.x);
@@ -396,10 +400,9 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                             acc0 = __fadd2_rn(acc0, pr);
                         pk[u] = pack_bf16x2(pr.x, pr.y);
                     }
-                    // the next 32 score columns (load and wait in one statement) before this
-                    // chunk's P goes to columns [16cc, 16cc+16), which were already read
-                    if (cc < 3) tmem_ld32p(tS + 32 * (cc + 1), sr + 32 * (cc + 1));
-                    tmem_st16(tS + cc * 16, pk);
+                    // P of chunk cc goes to columns [8cc, 8cc+8), scores that were already read
+                    if (cc < 7) tmem_ld16p(tS + 16 * (cc + 1), sr + 16 * (cc + 1));
+                    tmem_st8(tS + cc * 8, pk);
                 }
                 rs0 = acc0.x + acc1.x;
                 rs1 = acc0.y + acc1.y;

@@ -206,6 +206,19 @@ __device__ __forceinline__ void tmem_ld32p(uint32_t taddr, uint32_t *r) {
     tmem_ld32(taddr, *reinterpret_cast<uint32_t(*)[32]>(r));
 }
 
+// 32 lanes x 16 columns of 32 bit into a 16-register slice, load + wait fused.
+__device__ __forceinline__ void tmem_ld16p(uint32_t taddr, uint32_t *r) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+
 // Two 32-column loads in flight, one wait: columns [col, col+32) and [col2, col2+32).
 __device__ __forceinline__ void tmem_ld32x2(uint32_t taddr, uint32_t taddr2, uint32_t (&r)[32],
                                             uint32_t (&q)[32]) {
@@ -261,6 +274,12 @@ __device__ __forceinline__ void tmem_ld128(uint32_t taddr, uint32_t (&q)[128]) {
           "=r"(q[124]), "=r"(q[125]), "=r"(q[126]), "=r"(q[127])
         : "r"(taddr)
         : "memory");
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t *r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
 }
 
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
