@@ -292,23 +292,20 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 const bool more = j + 1 < nblk;
 #pragma unroll
                 for (int t = 0; t < NQT; ++t) {
-                    if (!mbar_wait_fast(p_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutP)) { ok = false; break; }
+                    // V_j and K_{j+1} are normally resident long before P_t(j): waiting for them
+                    // first keeps the P handoff the only wait between the softmax and the issue
                     if (t == 0 && !mbar_wait_fast(kv_full(sV), (iV / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
                         ok = false;
                         break;
                     }
+                    if (t == 0 && more && !mbar_wait_fast(kv_full(sK), (iK / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                        ok = false;
+                        break;
+                    }
+                    if (!mbar_wait_fast(p_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutP)) { ok = false; break; }
                     tc_fence_after();
                     issue_pv(t, sV, j > 0);
-                    if (more) {
-                        if (t == 0) {
-                            if (!mbar_wait_fast(kv_full(sK), (iK / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                        }
-                        issue_qk(t, sK);
-                    }
+                    if (more) issue_qk(t, sK);
                     tc_commit(s_full(t));
                 }
                 if (!ok) break;
