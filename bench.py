@@ -56,8 +56,13 @@ WORKLOADS = {
                                 "BASELINE config 2 at Sq=Sk=2048"),
     "qwen3_gqa_prefill_s1024": (32, 8, 1024, 1024, 128, 0, "normal", 1, (0.0, 1.0),
                                 "BASELINE config 2 at Sq=Sk=1024"),
+    "qwen3_gqa_prefill_s4096_causal": (32, 8, 4096, 4096, 128, 1, "normal", 1, (0.0, 1.0),
+                                       "BASELINE config 2 shape at S=4096 with causal masking (useful FLOPs)"),
     "mqa_prefill_b8_s2048": (8 * 16, 8, 2048, 2048, 128, 0, "uniform", 3, (-2.0, 2.0),
                              "BASELINE config 4 prefill: MQA 16/1 D128 batch 8 Sq=Sk=2048"),
+    "long_prefill_b4_s16384": (4 * 64, 4 * 8, 16384, 16384, 128, 0, "normal", 4, (0.0, 0.5),
+                               "BASELINE config 5 prefill: GQA 64/8 D128 batch 4 Sq=Sk=16384, N(0,0.5); "
+                               "one GPU runs every kv-head group (the multi-GPU run shards them)"),
     "gqa_decode_b64_sk8192": (64 * 32, 64 * 8, 1, 8192, 128, 0, "normal", 2, (0.0, 1.0),
                               "BASELINE config 3: GQA decode B64 Hq32/Hkv8 D128 Sq=1 Sk=8192"),
     "mqa_decode_b128_sk4096": (128 * 16, 128, 1, 4096, 128, 0, "uniform", 3, (-2.0, 2.0),

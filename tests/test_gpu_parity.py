@@ -113,6 +113,17 @@ def test_config5_long_decode_single_gpu(cuda_dev):
     check(ref, out, B * Hq, 1, D, rows, "config5 decode")
 
 
+def test_config5_long_prefill_single_gpu(cuda_dev):
+    """BASELINE config 5 prefill at batch 1 (bench: batch 4), Sq=Sk=16384, 64/8 heads, N(0,0.5)
+    seed 4: 128 key blocks per unit, spread rows checked against the fp32 reference."""
+    B, Hq, Hkv, S, D = 1, 64, 8, 16384, 128
+    Q, K, V = oracle.seeded_inputs(B * Hq, B * Hkv, S, S, D, seed=4, a=0.0, b=0.5)
+    rows = oracle.rowset(S, 6)
+    ref = oracle.attn_ref(Q, K, V, B * Hq, B * Hkv, S, S, D, 0, rows)
+    out = run_gpu(Q, K, V, B * Hq, B * Hkv, S, S, D, 0, dev=cuda_dev)
+    check(ref, out, B * Hq, S, D, rows, "config5 prefill")
+
+
 # --------------------------------------------------------------------- edge cases
 def test_sk1_is_v0_exactly(cuda_dev):
     """Sk=1: the one-element softmax is exactly 1, so O = V[0] bit for bit (EXEC_LOG F17)."""
