@@ -348,10 +348,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
         bool ok = true;
         const float2 c2 = make_float2(sl2, sl2);
         for (int j = 0; j < nblk; ++j) {
-            ok = mbar_wait(s_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutS);
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            tc_fence_after();
+            // The path decisions need no scores, so they are made before the wait.
             const long long key0 = kb0 + (long long)j * kBN;
             const long long nv = lastkey - key0 + 1;
             // `full`: every row of this warp sees every key of the block (no tail, no causal
@@ -364,6 +361,10 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             // does the warp redo the block exactly below (rare: the first block sets a max that
             // later blocks seldom exceed by that much).
             const bool spec = full && __all_sync(0xffffffffu, m != -INFINITY);
+            ok = mbar_wait(s_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutS);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            tc_fence_after();
             uint32_t sr[128];
             float rs0 = 0.f, rs1 = 0.f;
             bool redo = true;
