@@ -65,6 +65,10 @@ struct TcParams {
     int pieces, keys_per_piece;
     int row_base, part_rows;  // split units cover global rows [row_base, row_base + part_rows)
     int write_partials;
+    int n_items;  // work items (units, or units and key pieces); the grid has min(n_items, SMs) CTAs
+    int snake;    // 1: alternate the direction of the per-CTA item walk every round (causal)
+    int group;    // query heads per kv head
+    int head_units;  // causal: units per query head when every unit lies within one head, else 0
     float scale_log2;
 };
 
@@ -74,7 +78,7 @@ struct TcConfig {
     static constexpr int KVTILE = kBN * DP * 2;  // bytes of one K or V tile
     static constexpr int NS_RAW = (kSmemBudget - NQT * QTILE) / KVTILE;
     static constexpr int NS = NS_RAW > 8 ? 8 : NS_RAW;  // K/V ring slots
-    static constexpr int NBAR = 2 + 2 * NS + 2 * NQT;   // q_full, done, kv_full/empty, s/p_full
+    static constexpr int NBAR = 3 + 2 * NS + 3 * NQT;   // q_full/empty, done, kv_full/empty, s/p/o_full
     static constexpr int SMEM = 1024 + NQT * QTILE + NS * KVTILE + NBAR * 8 + 16;
     static constexpr int THREADS = 128 + 128 * NQT;
     static constexpr uint32_t TMEM_COLS = (NQT * kBN + NQT * DP) <= 256 ? 256u : 512u;
@@ -98,8 +102,14 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int *s
     }
 }
 
-// GENERAL=false: every CTA runs a whole unit and writes normalised O (plain prefill/decode
+// GENERAL=false: every work item is a whole unit that writes normalised O (plain prefill/decode
 // without splits); GENERAL=true adds key pieces and caller-partial output.
+//
+// Persistent: the grid has at most one CTA per SM and each CTA walks the work items
+// blockIdx.x, blockIdx.x + gridDim.x, ... (for causal masking in alternating directions over
+// the longest-first list, so the long and short units even out per CTA). Every barrier keeps
+// counting phases across items, so the next item's Q load, first QK and first softmax block
+// overlap the previous item's last PV and epilogue.
 template <int DP, int NQT, bool VT, bool GENERAL>
 __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -117,58 +127,81 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     const uint32_t sQ = base_u32;
     const uint32_t sKV = base_u32 + NQT * C::QTILE;
     const uint32_t bar0 = sKV + NS * C::KVTILE;
-    const uint32_t q_full = bar0;
-    const uint32_t done_bar = bar0 + 8;
-    auto kv_full = [&](int s) { return bar0 + 16 + 8u * s; };
-    auto kv_empty = [&](int s) { return bar0 + 16 + 8u * (NS + s); };
-    auto s_full = [&](int t) { return bar0 + 16 + 8u * (2 * NS + t); };
-    auto p_full = [&](int t) { return bar0 + 16 + 8u * (2 * NS + NQT + t); };
+    const uint32_t q_full = bar0;         // Q tiles of an item landed
+    const uint32_t q_empty = bar0 + 8;    // every QK of an item finished: Q may be reloaded
+    const uint32_t done_bar = bar0 + 16;
+    auto kv_full = [&](int s) { return bar0 + 24 + 8u * s; };
+    auto kv_empty = [&](int s) { return bar0 + 24 + 8u * (NS + s); };
+    auto s_full = [&](int t) { return bar0 + 24 + 8u * (2 * NS + t); };           // scores S_t ready
+    auto p_full = [&](int t) { return bar0 + 24 + 8u * (2 * NS + NQT + t); };     // P_t stored
+    auto o_full = [&](int t) { return bar0 + 24 + 8u * (2 * NS + 2 * NQT + t); }; // an item's O_t final
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + (bar0 - base_u32) + C::NBAR * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
 
-    // ---------------- work item
-    // Which unit (row tile of one kv head) and which key piece this CTA runs.
-    // !GENERAL: 2-D grid, one CTA per unit: (tiles, Hkv), or with causal masking (Hkv, tiles)
-    //   walked from the highest row tile down, so the longest units start first.
-    // GENERAL: 1-D grid over kv-major units; units below n_direct run whole, each later unit
-    //   runs as `pieces` key pieces.
-    int kv, tile, piece = -1;
-    if (!GENERAL) {
-        if (p.causal) {
-            kv = blockIdx.x;
-            tile = p.tiles_per_kv - 1 - (int)blockIdx.y;
+    // ---------------- work items
+    // Item index q -> unit (row tile of one kv head) and key piece.
+    // !GENERAL: non-causal q = kv * tiles + tile. Causal: a unit's key range grows with its query
+    //   position within its head (the group's heads are stacked in the packed rows), so q walks
+    //   the positions from the last down, every kv head and every query head of the group at
+    //   each position: the longest units come first.
+    // GENERAL: kv-major units; units below n_direct run whole, each later unit as `pieces` key
+    //   pieces.
+    struct Item {
+        int kv, row0, piece, kb0, kb1, nblk;
+    };
+    auto item_at = [&](int q) {
+        Item it;
+        int tile;
+        it.piece = -1;
+        if (!GENERAL) {
+            if (p.causal && p.head_units > 0) {
+                const int hk = p.Hkv * p.group;
+                const int rem = q % hk;
+                it.kv = rem % p.Hkv;
+                tile = (rem / p.Hkv) * p.head_units + (p.head_units - 1 - q / hk);
+            } else if (p.causal) {  // units straddle heads: highest row tile first
+                it.kv = q % p.Hkv;
+                tile = p.tiles_per_kv - 1 - q / p.Hkv;
+            } else {
+                it.kv = q / p.tiles_per_kv;
+                tile = q % p.tiles_per_kv;
+            }
         } else {
-            tile = blockIdx.x;
-            kv = blockIdx.y;
+            int u = q;
+            if (u >= p.n_direct) {
+                const int w = u - p.n_direct;
+                u = p.n_direct + w / p.pieces;
+                it.piece = w % p.pieces;
+            }
+            it.kv = u / p.tiles_per_kv;
+            tile = u % p.tiles_per_kv;
         }
-    } else {
-        int u = blockIdx.x;
-        if (u >= p.n_direct) {
-            const int q = u - p.n_direct;
-            u = p.n_direct + q / p.pieces;
-            piece = q % p.pieces;
+        it.row0 = tile * kBM * NQT;
+        it.kb0 = it.piece < 0 ? 0 : it.piece * p.keys_per_piece;  // local key range [kb0, kb1)
+        it.kb1 = it.piece < 0 ? p.Sk : min(p.Sk, it.kb0 + p.keys_per_piece);
+        int kend = it.kb1;
+        if (p.causal) {
+            const int rlast = min(it.row0 + kBM * NQT, p.rows_per_kv) - 1;
+            const int i_hi = (it.row0 / p.Sq == rlast / p.Sq) ? (rlast % p.Sq) : (p.Sq - 1);
+            const long long lim = (long long)p.Sk_total - p.Sq + i_hi - p.k_begin;  // last live local key
+            if (lim + 1 < (long long)kend) kend = (int)max(lim + 1, (long long)it.kb0);
         }
-        kv = u / p.tiles_per_kv;
-        tile = u % p.tiles_per_kv;
-    }
-    const int row0 = tile * kBM * NQT;
-    const int kb0 = piece < 0 ? 0 : piece * p.keys_per_piece;  // local key range [kb0, kb1)
-    const int kb1 = piece < 0 ? p.Sk : min(p.Sk, kb0 + p.keys_per_piece);
-    int kend = kb1;
-    if (p.causal) {
-        const int rlast = min(row0 + kBM * NQT, p.rows_per_kv) - 1;
-        const int i_hi = (row0 / p.Sq == rlast / p.Sq) ? (rlast % p.Sq) : (p.Sq - 1);
-        const long long lim = (long long)p.Sk_total - p.Sq + i_hi - p.k_begin;  // last live local key
-        if (lim + 1 < (long long)kend) kend = (int)max(lim + 1, (long long)kb0);
-    }
-    const int nblk = kend > kb0 ? (kend - kb0 + kBN - 1) / kBN : 0;
+        it.nblk = kend > it.kb0 ? (kend - it.kb0 + kBN - 1) / kBN : 0;
+        return it;
+    };
+    // this CTA's r-th item (or >= n_items when there is none)
+    auto item_index = [&](int r) {
+        const int G = (int)gridDim.x, b = (int)blockIdx.x;
+        return r * G + ((p.snake && (r & 1)) ? (G - 1 - b) : b);
+    };
 
     // ---------------- setup
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
         mbar_init(done_bar, 1);
         for (int s = 0; s < NS; ++s) {
             mbar_init(kv_full(s), 1);
@@ -177,6 +210,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
         for (int t = 0; t < NQT; ++t) {
             mbar_init(s_full(t), 1);
             mbar_init(p_full(t), 128);
+            mbar_init(o_full(t), 1);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -197,57 +231,75 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
 
     // Register budgets per warpgroup (NQT=2 launches 384 threads x 168 registers): the
     // producer/MMA warpgroup gives registers up, the two softmax warpgroups take them:
-    // 128 x 56 + 256 x 224 = 64512 = 384 x 168.
+    // 128 x 128 + 256 x 184 = 63488 <= 384 x 168 = 64512 (neither side spills).
     if (warp < 4) {
-        if constexpr (NQT == 2) regs_dec<112>();
+        if constexpr (NQT == 2) regs_dec<128>();
     if (warp == 0) {
         // ============================ TMA producer
-        if (lane == 0 && nblk > 0) {
-            int issued = 0;
-            bool ok = true;
-            mbar_expect_tx(q_full, NQT * C::QTILE);
-#pragma unroll
-            for (int t = 0; t < NQT; ++t)
-#pragma unroll
-                for (int b = 0; b < NBOX_D; ++b)
-                    tma_load_3d(sQ + t * C::QTILE + b * BOX_ROWS128, &tmQ, q_full, b * 64,
-                                row0 + t * kBM, kv);
-            const int nload = 2 * nblk;
-            for (int i = 0; i < nload; ++i) {
-                const int slot = i % NS;
-                const int round = i / NS;
-                if (round > 0 &&
-                    !mbar_wait(kv_empty(slot), (round - 1) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+        if (lane == 0) {
+            uint32_t gl = 0;   // K/V tile loads issued, over all items
+            int qi = 0;        // items with at least one key block, so far
+            bool ok = true, q_inflight = false;
+            for (int r = 0; ok; ++r) {
+                const int q = item_index(r);
+                if (q >= p.n_items) break;
+                const Item it = item_at(q);
+                if (it.nblk == 0) continue;
+                const int kv = it.kv, kb0 = it.kb0;
+                // the previous item's QKs have all finished reading Q
+                if (qi > 0 && !mbar_wait(q_empty, (qi - 1) & 1, abort_flag, p.status, kDevErrTimeoutQ)) {
                     ok = false;
                     break;
                 }
-                const int key0 = kb0 + (i >> 1) * kBN;
-                const uint32_t dst = sKV + slot * C::KVTILE;
-                const uint32_t bar = kv_full(slot);
-                mbar_expect_tx(bar, C::KVTILE);
-                if ((i & 1) == 0) {
+                mbar_expect_tx(q_full, NQT * C::QTILE);
+#pragma unroll
+                for (int t = 0; t < NQT; ++t)
 #pragma unroll
                     for (int b = 0; b < NBOX_D; ++b)
-                        tma_load_3d(dst + b * (kBN * 128), &tmK, bar, b * 64, key0, kv);
-                } else if (!VT) {
+                        tma_load_3d(sQ + t * C::QTILE + b * BOX_ROWS128, &tmQ, q_full, b * 64,
+                                    it.row0 + t * kBM, kv);
+                q_inflight = true;
+                const int nload = 2 * it.nblk;
+                for (int i = 0; i < nload; ++i, ++gl) {
+                    const int slot = gl % NS;
+                    const int round = gl / NS;
+                    if (round > 0 &&
+                        !mbar_wait(kv_empty(slot), (round - 1) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                        ok = false;
+                        break;
+                    }
+                    const int key0 = kb0 + (i >> 1) * kBN;
+                    const uint32_t dst = sKV + slot * C::KVTILE;
+                    const uint32_t bar = kv_full(slot);
+                    mbar_expect_tx(bar, C::KVTILE);
+                    if ((i & 1) == 0) {
 #pragma unroll
-                    for (int b = 0; b < NBOX_D; ++b)
-                        tma_load_3d(dst + b * (kBN * 128), &tmV, bar, b * 64, key0, kv);
-                } else {
+                        for (int b = 0; b < NBOX_D; ++b)
+                            tma_load_3d(dst + b * (kBN * 128), &tmK, bar, b * 64, key0, kv);
+                    } else if (!VT) {
 #pragma unroll
-                    for (int b = 0; b < kBN / 64; ++b)
-                        tma_load_3d(dst + b * (DP * 128), &tmV, bar, key0 + b * 64, 0, kv);
+                        for (int b = 0; b < NBOX_D; ++b)
+                            tma_load_3d(dst + b * (kBN * 128), &tmV, bar, b * 64, key0, kv);
+                    } else {
+#pragma unroll
+                        for (int b = 0; b < kBN / 64; ++b)
+                            tma_load_3d(dst + b * (DP * 128), &tmV, bar, key0 + b * 64, 0, kv);
+                    }
                 }
-                issued = i + 1;
+                if (ok) {
+                    q_inflight = false;
+                    ++qi;
+                }
             }
             if (!ok) {  // let the copies already in flight land before the CTA exits
-                drain_wait(q_full, 0, p.status);
-                for (int i = max(0, issued - NS); i < issued; ++i) drain_wait(kv_full(i % NS), (i / NS) & 1, p.status);
+                if (q_inflight) drain_wait(q_full, qi & 1, p.status);
+                for (uint32_t i = gl > (uint32_t)NS ? gl - NS : 0u; i < gl; ++i)
+                    drain_wait(kv_full(i % NS), (i / NS) & 1, p.status);
             }
         }
     } else if (warp == 1) {
         // ============================ MMA issuer (one thread)
-        if (lane == 0 && nblk > 0) {
+        if (lane == 0) {
             constexpr uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, 0, 0);
             constexpr uint32_t idesc_pv = idesc_bf16_f32(kBM, DP, 0, VT ? 0 : 1);
             auto issue_qk = [&](int t, int slot) {
@@ -275,42 +327,67 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                     umma_ts(d_tmem, a_tmem + ks * 8, bdesc, idesc_pv, (accumulate || ks > 0) ? 1u : 0u);
                 }
             };
-            bool ok = mbar_wait_fast(q_full, 0, abort_flag, p.status, kDevErrTimeoutQ) &&
-                      mbar_wait_fast(kv_full(0), 0, abort_flag, p.status, kDevErrTimeoutKV);
-            if (ok) {
+            uint32_t gc = 0;   // K/V tiles consumed, over all items
+            uint32_t pp = 0;   // P handoffs consumed per tile, over all items
+            int qi = 0;
+            bool ok = true;
+            for (int r = 0; ok; ++r) {
+                const int q = item_index(r);
+                if (q >= p.n_items) break;
+                const Item it = item_at(q);
+                const int nblk = it.nblk;
+                if (nblk == 0) continue;
+                const uint32_t sK0 = gc % NS;
+                ok = mbar_wait_fast(q_full, qi & 1, abort_flag, p.status, kDevErrTimeoutQ) &&
+                     mbar_wait_fast(kv_full(sK0), (gc / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV);
+                if (!ok) break;
                 tc_fence_after();
 #pragma unroll
                 for (int t = 0; t < NQT; ++t) {
-                    issue_qk(t, 0);
+                    issue_qk(t, sK0);
                     tc_commit(s_full(t));
                 }
-                tc_commit(kv_empty(0));
-            }
-            for (int j = 0; ok && j < nblk; ++j) {
-                const int iV = 2 * j + 1, iK = 2 * j + 2;
-                const int sV = iV % NS, sK = iK % NS;
-                const bool more = j + 1 < nblk;
+                tc_commit(kv_empty(sK0));
+                if (nblk == 1) tc_commit(q_empty);
+                for (int j = 0; ok && j < nblk; ++j) {
+                    const uint32_t iV = gc + 2 * j + 1, iK = gc + 2 * j + 2;
+                    const int sV = iV % NS, sK = iK % NS;
+                    const bool more = j + 1 < nblk;
 #pragma unroll
-                for (int t = 0; t < NQT; ++t) {
-                    // V_j and K_{j+1} are normally resident long before P_t(j): waiting for them
-                    // first keeps the P handoff the only wait between the softmax and the issue
-                    if (t == 0 && !mbar_wait_fast(kv_full(sV), (iV / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
-                        ok = false;
-                        break;
+                    for (int t = 0; t < NQT; ++t) {
+                        // V_j and K_{j+1} are normally resident long before P_t(j): waiting for
+                        // them first keeps the P handoff the only wait between the softmax and
+                        // the issue
+                        if (t == 0 && !mbar_wait_fast(kv_full(sV), (iV / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                            ok = false;
+                            break;
+                        }
+                        if (t == 0 && more &&
+                            !mbar_wait_fast(kv_full(sK), (iK / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                            ok = false;
+                            break;
+                        }
+                        if (!mbar_wait_fast(p_full(t), pp & 1, abort_flag, p.status, kDevErrTimeoutP)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        issue_pv(t, sV, j > 0);
+                        if (more) {
+                            issue_qk(t, sK);
+                            tc_commit(s_full(t));
+                        } else {
+                            tc_commit(o_full(t));  // the item's O_t is final
+                        }
                     }
-                    if (t == 0 && more && !mbar_wait_fast(kv_full(sK), (iK / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
-                        ok = false;
-                        break;
-                    }
-                    if (!mbar_wait_fast(p_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutP)) { ok = false; break; }
-                    tc_fence_after();
-                    issue_pv(t, sV, j > 0);
-                    if (more) issue_qk(t, sK);
-                    tc_commit(s_full(t));
+                    if (!ok) break;
+                    ++pp;
+                    tc_commit(kv_empty(sV));
+                    if (more) tc_commit(kv_empty(sK));
+                    if (j == nblk - 2) tc_commit(q_empty);  // the item's last QKs were just issued
                 }
-                if (!ok) break;
-                tc_commit(kv_empty(sV));
-                if (more) tc_commit(kv_empty(sK));
+                gc += 2 * nblk;
+                ++qi;
             }
             // Every MMA issued above must finish before TMEM is released.
             tc_commit(done_bar);
@@ -327,26 +404,33 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             tmem_dealloc(tmem_base, C::TMEM_COLS);
         }
     } else {
-        if constexpr (NQT == 2) regs_inc<192>();
+        if constexpr (NQT == 2) regs_inc<184>();
         // ============================ softmax / correction / epilogue
         const int t = (warp - 4) >> 2;
         const int quad = warp & 3;
         const int r = quad * 32 + lane;
+        const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        const uint32_t tS = tmem_base + lane_off + t * kBN;
+        const uint32_t tO = tmem_base + lane_off + NQT * kBN + t * DP;
+        const float sl2 = p.scale_log2;
+        const float2 c2 = make_float2(sl2, sl2);
+        uint32_t sp = 0;  // score-tile phases consumed, over all items
+        uint32_t op = 0;  // items finished (o_full phases consumed)
+        bool ok = true;
+        for (int ri = 0; ok; ++ri) {
+        const int qidx = item_index(ri);
+        if (qidx >= p.n_items) break;
+        const Item it = item_at(qidx);
+        const int kv = it.kv, row0 = it.row0, piece = it.piece, kb0 = it.kb0, kb1 = it.kb1, nblk = it.nblk;
         const int prow = row0 + t * kBM + r;  // packed row within this kv head
         const bool valid = prow < p.rows_per_kv;
         const int ipos = valid ? prow % p.Sq : 0;
         const long long lim = p.causal ? ((long long)p.Sk_total - p.Sq + ipos - p.k_begin)
                                        : (long long)(p.Sk - 1);  // last live local key of this row
         const long long lastkey = min(lim, (long long)kb1 - 1);
-        const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-        const uint32_t tS = tmem_base + lane_off + t * kBN;
-        const uint32_t tO = tmem_base + lane_off + NQT * kBN + t * DP;
-        const float sl2 = p.scale_log2;
 
         float m = -INFINITY, l = 0.f;
         float ms = 0.f;  // m * scale_log2, rounded once (0 while m is -inf)
-        bool ok = true;
-        const float2 c2 = make_float2(sl2, sl2);
         for (int j = 0; j < nblk; ++j) {
             // The path decisions need no scores, so they are made before the wait.
             const long long key0 = kb0 + (long long)j * kBN;
@@ -361,7 +445,8 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             // does the warp redo the block exactly below (rare: the first block sets a max that
             // later blocks seldom exceed by that much).
             const bool spec = full && __all_sync(0xffffffffu, m != -INFINITY);
-            ok = mbar_wait(s_full(t), j & 1, abort_flag, p.status, kDevErrTimeoutS);
+            ok = mbar_wait(s_full(t), sp & 1, abort_flag, p.status, kDevErrTimeoutS);
+            ++sp;
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
             tc_fence_after();
@@ -508,7 +593,8 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
         }
         bool have_o = false;
         if (ok && nblk > 0) {
-            have_o = mbar_wait(s_full(t), nblk & 1, abort_flag, p.status, kDevErrTimeoutS);
+            have_o = mbar_wait(o_full(t), op & 1, abort_flag, p.status, kDevErrTimeoutS);
+            ++op;
             have_o = __all_sync(0xffffffffu, have_o);
             ok = have_o;
             if (have_o) tc_fence_after();
@@ -555,6 +641,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                     }
                 }
             }
+        }
         }
         // teardown (softmax warpgroups): TMEM reads done before the dealloc below
         tc_fence_before();
@@ -655,12 +742,17 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     prm.part_rows = P->Hq * P->Sq - P->row_base;
     prm.write_partials = P->write_partials;
     prm.scale_log2 = P->scale_log2;
+    prm.group = group;
+    prm.head_units = (P->Sq % (kBM * NQT) == 0) ? P->Sq / (kBM * NQT) : 0;
+    const int sms = ts_num_sms() > 0 ? ts_num_sms() : 1;
     if (prm.n_direct == units && !prm.write_partials) {
-        const dim3 grid = prm.causal ? dim3(P->Hkv, tiles_per_kv) : dim3(tiles_per_kv, P->Hkv);
-        return launch_tc_inst<DP, NQT, VT, false>(st, tmQ, tmK, tmV, prm, grid);
+        prm.n_items = units;
+        prm.snake = prm.causal;
+        return launch_tc_inst<DP, NQT, VT, false>(st, tmQ, tmK, tmV, prm, dim3(min(units, sms)));
     }
-    return launch_tc_inst<DP, NQT, VT, true>(st, tmQ, tmK, tmV, prm,
-                                             dim3(prm.n_direct + (units - prm.n_direct) * prm.pieces));
+    prm.n_items = prm.n_direct + (units - prm.n_direct) * prm.pieces;
+    prm.snake = 0;
+    return launch_tc_inst<DP, NQT, VT, true>(st, tmQ, tmK, tmV, prm, dim3(min(prm.n_items, sms)));
 }
 
 static int nqt_for(const fa_problem *P) {
