@@ -99,6 +99,19 @@ int attn_flash_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V, f
                       int Hq, int Hkv, int Sq, int Sk, int D, int causal, int bk,
                       void *scratch, int v_prepacked, void *stream);
 
+/* Output element types of attn_flash_stream_out. */
+#define ATTN_OUT_F32 0  /* fp32, the reference's O (flash.c:727-729) */
+#define ATTN_OUT_BF16 1 /* bf16 bit patterns, rounded as flash.c:78-92 rounds P */
+
+/* attn_flash_stream with a choice of output element type: out_dtype ATTN_OUT_F32 is exactly
+ * attn_flash_stream; ATTN_OUT_BF16 writes O as uint16_t bf16 bits [Hq][Sq][D] (round to
+ * nearest even, NaN/Inf passed through), halving the output bytes: each element equals the
+ * rounding of what the fp32 call returns. An extension of the reference's interface, which
+ * writes fp32 O only (flash.c:727-729); any other out_dtype returns ATTN_ERR_ARGS. */
+int attn_flash_stream_out(const uint16_t *Q, const uint16_t *K, const uint16_t *V, void *O,
+                          int out_dtype, int Hq, int Hkv, int Sq, int Sk, int D, int causal, int bk,
+                          void *scratch, int v_prepacked, void *stream);
+
 /* Synchronises `stream`, reads and clears the device status word in `scratch`.
  * Returns ATTN_OK, or ATTN_ERR_DEVICE when a kernel on that scratch reported a failure
  * (the raw device code goes to *device_code when non-NULL), or ATTN_ERR_CUDA. */

@@ -107,6 +107,14 @@ def test_argument_validation_before_any_gpu_work(built_lib, bad):
     assert _lib_call(**bad) == ts.ATTN_ERR_ARGS
 
 
+@pytest.mark.parametrize("out_dtype", [-1, 2, 7])
+def test_bad_output_type_is_rejected(built_lib, out_dtype):
+    L = ts.load_library()
+    rc = L.attn_flash_stream_out(1 << 20, 1 << 20, 1 << 20, 1 << 20, out_dtype, 8, 2, 16, 16, 64, 0, 128, 1 << 20, 0,
+                                 None)
+    assert rc == ts.ATTN_ERR_ARGS
+
+
 def test_misaligned_scratch(built_lib):
     assert _lib_call(scratch=(1 << 20) + 4) == ts.ATTN_ERR_ALIGN
 

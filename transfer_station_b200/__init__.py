@@ -23,6 +23,9 @@ ATTN_GPU_KEY_TILE = 128
 ATTN_D_MAX = 256
 ATTN_PARTIAL_ROWS = 65536
 
+ATTN_OUT_F32 = 0
+ATTN_OUT_BF16 = 1
+
 ATTN_OK = 0
 ATTN_ERR_ARGS = -1
 ATTN_ERR_ALIGN = -2
@@ -41,6 +44,8 @@ EXPORTS = {
     "attn_flash_stream": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 7 + [ctypes.c_void_p,
                                                                                           ctypes.c_int,
                                                                                           ctypes.c_void_p]),
+    "attn_flash_stream_out": (ctypes.c_int, [_u16p, _u16p, _u16p, ctypes.c_void_p, ctypes.c_int] + [ctypes.c_int] * 7 +
+                              [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "attn_flash_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
     "attn_flash_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "attn_flash_kernel_launches": (ctypes.c_ulonglong, []),
@@ -116,6 +121,15 @@ def attn_flash_stream(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_pre
     return int(load_library().attn_flash_stream(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), Hq, Hkv, Sq, Sk, D,
                                                  int(causal), bk, _ptr(scratch), int(v_prepacked),
                                                  _stream_handle(stream)))
+
+
+def attn_flash_stream_out(Q, K, V, O, out_dtype, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_prepacked=0,
+                          stream=None) -> int:
+    """attn_flash_stream with a choice of output type: ATTN_OUT_F32 (O float32) or ATTN_OUT_BF16
+    (O int16/uint16 holding bf16 bits, rounded to nearest even). Returns the status."""
+    return int(load_library().attn_flash_stream_out(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), int(out_dtype), Hq, Hkv,
+                                                     Sq, Sk, D, int(causal), bk, _ptr(scratch), int(v_prepacked),
+                                                     _stream_handle(stream)))
 
 
 def attn_flash(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_prepacked=0) -> None:

@@ -204,6 +204,20 @@ int attn_flash_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V, f
     return ts_run(&p, scratch, stream);
 }
 
+int attn_flash_stream_out(const uint16_t *Q, const uint16_t *K, const uint16_t *V, void *O, int out_dtype, int Hq,
+                          int Hkv, int Sq, int Sk, int D, int causal, int bk, void *scratch, int v_prepacked,
+                          void *stream) {
+    attn_bk_check(bk, "attn_flash");
+    if (!O || (out_dtype != ATTN_OUT_F32 && out_dtype != ATTN_OUT_BF16)) return ATTN_ERR_ARGS;
+    int rc = ts_validate(Q, K, V, Hq, Hkv, Sq, Sk, D, scratch);
+    if (rc != ATTN_OK) return rc;
+    fa_problem p;
+    ts_fill(&p, Q, K, V, Hq, Hkv, Sq, Sk, D, causal, v_prepacked);
+    p.O = (float *)O;
+    p.o_bf16 = out_dtype == ATTN_OUT_BF16;
+    return ts_run(&p, scratch, stream);
+}
+
 int attn_flash_partial_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *m, float *l,
                               float *acc, int Hq, int Hkv, int Sq, int Sk_local, int Sk_total, int k_begin, int D,
                               int causal, int bk, void *scratch, int v_prepacked, void *stream) {
@@ -226,7 +240,7 @@ int attn_flash_combine_stream(const float *m, const float *l, const float *acc, 
                               float *O, void *stream) {
     if (!m || !l || !acc || !O || nparts < 1 || rows < 0 || D < 1 || D > ATTN_D_MAX) return ATTN_ERR_ARGS;
     if (ts_cc_major() != 10) return ATTN_ERR_NOT_SM100;
-    return ts_launch_combine(m, l, acc, nparts, rows, D, O, NULL, NULL, stream);
+    return ts_launch_combine(m, l, acc, nparts, rows, D, O, NULL, NULL, 0, stream);
 }
 
 int attn_flash_status(void *scratch, void *stream, int *device_code) {

@@ -14,6 +14,7 @@
 
 #include "attn_flash.h"
 #include "fa_launch.h"
+#include "sm100_ptx.cuh"
 
 extern "C" int ts_launch_tc(const fa_problem *P, void *stream);
 
@@ -39,7 +40,7 @@ struct SimtParams {
     const uint16_t *Q, *K, *V;
     float *O, *part_m, *part_l, *part_acc;
     int Hq, Hkv, Sq, Sk, Sk_total, k_begin, D, causal, v_prepacked;
-    int keys_per_split, partial;
+    int keys_per_split, partial, o_bf16;
     float scale_log2;
 };
 
@@ -114,7 +115,12 @@ __global__ void __launch_bounds__(256) fa_simt_kernel(const SimtParams p) {
 #pragma unroll
         for (int u = 0; u < kSimtMaxU; ++u) {
             const int c = lane + 32 * u;
-            if (c < p.D) p.O[grow * p.D + c] = acc[u] * inv;
+            if (c < p.D) {
+                if (p.o_bf16)
+                    reinterpret_cast<uint16_t *>(p.O)[grow * p.D + c] = (uint16_t)f32_to_bf16_bits(acc[u] * inv);
+                else
+                    p.O[grow * p.D + c] = acc[u] * inv;
+            }
         }
     }
 }
@@ -128,7 +134,7 @@ template <bool VEC>
 __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict__ m, const float *__restrict__ l,
                                                          const float *__restrict__ acc, int nparts, int rows, int D,
                                                          float *__restrict__ out, float *__restrict__ out_m,
-                                                         float *__restrict__ out_l) {
+                                                         float *__restrict__ out_l, int out_bf16) {
     const int lane = threadIdx.x & 31;
     const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= rows) return;
@@ -157,7 +163,13 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict
                 a.z = fmaf(w, x.z, a.z);
                 a.w = fmaf(w, x.w, a.w);
             }
-            *reinterpret_cast<float4 *>(out + (size_t)r * D + c) = make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
+            if (out_bf16)  // out holds bf16 bits; D % 4 == 0 keeps the 8-byte store aligned
+                *reinterpret_cast<uint2 *>(reinterpret_cast<uint16_t *>(out) + (size_t)r * D + c) =
+                    make_uint2(f32_to_bf16_bits(a.x * inv) | (f32_to_bf16_bits(a.y * inv) << 16),
+                               f32_to_bf16_bits(a.z * inv) | (f32_to_bf16_bits(a.w * inv) << 16));
+            else
+                *reinterpret_cast<float4 *>(out + (size_t)r * D + c) =
+                    make_float4(a.x * inv, a.y * inv, a.z * inv, a.w * inv);
         }
     } else {
         for (int c = lane; c < D; c += 32) {
@@ -168,7 +180,10 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict
                 const float w = (ms != -INFINITY) ? ex2f(ms - mx) : 0.f;
                 a = fmaf(w, acc[((size_t)s * rows + r) * D + c], a);
             }
-            out[(size_t)r * D + c] = a * inv;
+            if (out_bf16)
+                reinterpret_cast<uint16_t *>(out)[(size_t)r * D + c] = (uint16_t)f32_to_bf16_bits(a * inv);
+            else
+                out[(size_t)r * D + c] = a * inv;
         }
     }
     if (out_m && lane == 0) {
@@ -202,17 +217,19 @@ extern "C" int ts_cc_major(void) {
 }
 
 extern "C" int ts_launch_combine(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
-                                 float *O, float *out_m, float *out_l, void *stream) {
+                                 float *O, float *out_m, float *out_l, int out_bf16, void *stream) {
     if (rows <= 0) return ATTN_OK;
     const int warps = 8;
     dim3 grid((rows + warps - 1) / warps);
     const bool vec = (D % 4 == 0) && ((((uintptr_t)acc) | ((uintptr_t)O)) & 15u) == 0;
     if (vec)
         ts::fa_combine_kernel<true><<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows,
-                                                                                               D, O, out_m, out_l);
+                                                                                               D, O, out_m, out_l,
+                                                                                               out_bf16);
     else
         ts::fa_combine_kernel<false><<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows,
-                                                                                                D, O, out_m, out_l);
+                                                                                                D, O, out_m, out_l,
+                                                                                                out_bf16);
     if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
     ts_count_launch();
     return ATTN_OK;
@@ -238,6 +255,7 @@ static int launch_simt(const fa_problem *P, void *stream, int partial) {
     s.v_prepacked = P->v_prepacked;
     s.keys_per_split = P->keys_per_split;
     s.partial = partial;
+    s.o_bf16 = P->o_bf16;
     s.scale_log2 = P->scale_log2;
     const long long rows = (long long)P->Hq * P->Sq;
     const int warps = 8;
@@ -255,10 +273,14 @@ extern "C" int ts_launch_attention(const fa_problem *P, void *stream) {
     // merge the key pieces of the split rows [base, Hq*Sq) (all rows on the general path)
     const int rows = P->Hq * P->Sq;
     const int base = tc ? P->row_base : 0;
-    float *out = (P->write_partials ? P->out_acc : P->O) + (size_t)base * P->D;
+    const int obf = P->write_partials ? 0 : P->o_bf16;
+    float *out = P->write_partials ? P->out_acc + (size_t)base * P->D
+                                   : (obf ? reinterpret_cast<float *>(reinterpret_cast<uint16_t *>(P->O) +
+                                                                      (size_t)base * P->D)
+                                          : P->O + (size_t)base * P->D);
     return ts_launch_combine(P->part_m, P->part_l, P->part_acc, P->nsplit, rows - base, P->D, out,
                              P->write_partials ? P->out_m + base : nullptr,
-                             P->write_partials ? P->out_l + base : nullptr, stream);
+                             P->write_partials ? P->out_l + base : nullptr, obf, stream);
 }
 
 extern "C" int ts_clear_status(int *status, void *stream) {

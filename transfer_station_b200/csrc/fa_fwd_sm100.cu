@@ -65,6 +65,7 @@ struct TcParams {
     int pieces, keys_per_piece;
     int row_base, part_rows;  // split units cover global rows [row_base, row_base + part_rows)
     int write_partials;
+    int o_bf16;   // 1: O is bf16 bits (round to nearest even), else fp32
     int n_items;  // work items (units, or units and key pieces); the grid has min(n_items, SMs) CTAs
     int snake;    // 1: alternate the direction of the per-CTA item walk every round (causal)
     int group;    // query heads per kv head
@@ -605,6 +606,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             const size_t grow = (size_t)kv * p.rows_per_kv + prow;  // row of [Hq*Sq]
             float *dst;
             float mult;
+            bool out_bf16 = false;
             if (GENERAL && (piece >= 0 || p.write_partials)) {
                 // (m, l, unnormalised acc): a key piece's slot, or the caller's partial row
                 const size_t slot = piece >= 0 ? (size_t)piece * p.part_rows + (grow - p.row_base) : grow;
@@ -617,8 +619,9 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 dst = (piece >= 0 ? p.part_acc : p.out_acc) + slot * D;
                 mult = 1.f;
             } else {
-                dst = p.O + grow * D;
+                dst = p.O + grow * D;  // bf16 output: element offsets of a uint16_t array
                 mult = (l > 0.f) ? 1.f / l : 0.f;
+                out_bf16 = p.o_bf16 != 0;
             }
 #pragma unroll
             for (int cc = 0; cc < DP / 32; ++cc) {
@@ -636,7 +639,14 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                         if (c < D) {
                             float4 w = make_float4(u2f(o[4 * v]) * mult, u2f(o[4 * v + 1]) * mult,
                                                    u2f(o[4 * v + 2]) * mult, u2f(o[4 * v + 3]) * mult);
-                            *reinterpret_cast<float4 *>(dst + c) = w;
+                            if (out_bf16) {
+                                uint16_t *ob = reinterpret_cast<uint16_t *>(p.O) + grow * D + c;
+                                *reinterpret_cast<uint2 *>(ob) =
+                                    make_uint2(f32_to_bf16_bits(w.x) | (f32_to_bf16_bits(w.y) << 16),
+                                               f32_to_bf16_bits(w.z) | (f32_to_bf16_bits(w.w) << 16));
+                            } else {
+                                *reinterpret_cast<float4 *>(dst + c) = w;
+                            }
                         }
                     }
                 }
@@ -741,6 +751,7 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     prm.row_base = P->row_base;
     prm.part_rows = P->Hq * P->Sq - P->row_base;
     prm.write_partials = P->write_partials;
+    prm.o_bf16 = P->o_bf16;
     prm.scale_log2 = P->scale_log2;
     prm.group = group;
     prm.head_units = (P->Sq % (kBM * NQT) == 0) ? P->Sq / (kBM * NQT) : 0;

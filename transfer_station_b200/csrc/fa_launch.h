@@ -28,6 +28,7 @@ typedef struct fa_problem {
     int Hq, Hkv, Sq, Sk;       /* Sk = keys present in K/V (local shard length) */
     int Sk_total, k_begin;     /* global key axis length and this shard's first key */
     int D, causal, v_prepacked;
+    int o_bf16;                /* 1: O holds bf16 bits [Hq][Sq][D] (RNE as flash.c:78-92), else fp32 */
     int nsplit;                /* >1: split the key range, write partials, then combine */
     int keys_per_split;        /* multiple of the key tile */
     int write_partials;        /* 1: leave the result as (m, l, acc) partials, no combine */
@@ -59,7 +60,7 @@ int ts_launch_attention(const fa_problem *p, void *stream);
 
 /* Launch the combine kernel alone on partial arrays. */
 int ts_launch_combine(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
-                      float *O, float *out_m, float *out_l, void *stream);
+                      float *O, float *out_m, float *out_l, int out_bf16, void *stream);
 
 /* Zero the device status word (async). */
 int ts_clear_status(int *status, void *stream);

@@ -357,6 +357,14 @@ __device__ __forceinline__ float2 exp2_fma2(float2 x) {
                        __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
 }
 
+// fp32 -> bf16 bits exactly as flash.c:78-92 rounds: NaN and Inf pass through truncated,
+// everything else rounds to nearest even.
+__device__ __forceinline__ uint32_t f32_to_bf16_bits(float f) {
+    const uint32_t x = __float_as_uint(f);
+    if (((x >> 23) & 0xffu) == 0xffu) return x >> 16;
+    return (x + 0x7fffu + ((x >> 16) & 1u)) >> 16;
+}
+
 // Two floats -> packed bf16x2, round-to-nearest-even; `lo` lands in bits [15:0].
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
