@@ -112,6 +112,22 @@ int attn_flash_stream_out(const uint16_t *Q, const uint16_t *K, const uint16_t *
                           int out_dtype, int Hq, int Hkv, int Sq, int Sk, int D, int causal, int bk,
                           void *scratch, int v_prepacked, void *stream);
 
+/* Attention over a paged K/V cache (decode, or a few new query positions per sequence). No
+ * counterpart in the reference, whose K and V are contiguous (flash.c:727-729): this is the
+ * serving-side layout. B sequences; Q [B*Hq][Sq][D] and O [B*Hq][Sq][D] (fp32) as in
+ * attn_flash with batch folded into heads; K_pages and V_pages are pools
+ * [num_pages][Hkv][page_size][D] of bf16 bits; sequence b's keys are, in order, the rows of
+ * pages block_table[b * max_pages + 0 ..] and it has seq_lens[b] of them (clamped to
+ * [0, max_pages * page_size]; a sequence with none gets zero rows). block_table and seq_lens
+ * are device int arrays. causal: query i of sequence b sees keys 0 .. seq_lens[b] - Sq + i.
+ * page_size is 8, 16, 32, 64 or a multiple of 128; D a multiple of 8 up to 128; all pointers
+ * 16-byte aligned. A page id outside [0, num_pages) is caught by the kernel: it stops and
+ * attn_flash_status returns ATTN_ERR_DEVICE. Scratch as for attn_flash_stream. */
+int attn_flash_paged_stream(const uint16_t *Q, const uint16_t *K_pages, const uint16_t *V_pages,
+                            const int *block_table, const int *seq_lens, float *O, int B, int Hq,
+                            int Hkv, int Sq, int D, int causal, int page_size, int num_pages,
+                            int max_pages, void *scratch, void *stream);
+
 /* Synchronises `stream`, reads and clears the device status word in `scratch`.
  * Returns ATTN_OK, or ATTN_ERR_DEVICE when a kernel on that scratch reported a failure
  * (the raw device code goes to *device_code when non-NULL), or ATTN_ERR_CUDA. */

@@ -115,6 +115,17 @@ def test_bad_output_type_is_rejected(built_lib, out_dtype):
     assert rc == ts.ATTN_ERR_ARGS
 
 
+@pytest.mark.parametrize("bad", [dict(ps=24), dict(ps=0), dict(ps=200), dict(D=72 + 64), dict(D=36), dict(B=0),
+                                 dict(Hq=6, Hkv=4), dict(npages=0), dict(maxp=0)])
+def test_paged_argument_validation(built_lib, bad):
+    a = dict(ps=16, D=128, B=2, Hq=8, Hkv=2, npages=4, maxp=2)
+    a.update(bad)
+    L = ts.load_library()
+    rc = L.attn_flash_paged_stream(1 << 20, 1 << 20, 1 << 20, 1 << 20, 1 << 20, 1 << 20, a["B"], a["Hq"], a["Hkv"], 1,
+                                   a["D"], 0, a["ps"], a["npages"], a["maxp"], 1 << 20, None)
+    assert rc == ts.ATTN_ERR_ARGS
+
+
 def test_misaligned_scratch(built_lib):
     assert _lib_call(scratch=(1 << 20) + 4) == ts.ATTN_ERR_ALIGN
 

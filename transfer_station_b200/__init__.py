@@ -46,6 +46,8 @@ EXPORTS = {
                                                                                           ctypes.c_void_p]),
     "attn_flash_stream_out": (ctypes.c_int, [_u16p, _u16p, _u16p, ctypes.c_void_p, ctypes.c_int] + [ctypes.c_int] * 7 +
                               [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "attn_flash_paged_stream": (ctypes.c_int, [_u16p, _u16p, _u16p, ctypes.c_void_p, ctypes.c_void_p, _f32p] +
+                                [ctypes.c_int] * 9 + [ctypes.c_void_p, ctypes.c_void_p]),
     "attn_flash_status": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_int)]),
     "attn_flash_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "attn_flash_kernel_launches": (ctypes.c_ulonglong, []),
@@ -130,6 +132,15 @@ def attn_flash_stream_out(Q, K, V, O, out_dtype, Hq, Hkv, Sq, Sk, D, causal, bk,
     return int(load_library().attn_flash_stream_out(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), int(out_dtype), Hq, Hkv,
                                                      Sq, Sk, D, int(causal), bk, _ptr(scratch), int(v_prepacked),
                                                      _stream_handle(stream)))
+
+
+def attn_flash_paged_stream(Q, K_pages, V_pages, block_table, seq_lens, O, B, Hq, Hkv, Sq, D, causal, page_size,
+                            num_pages, max_pages, scratch, stream=None) -> int:
+    """Attention over a paged K/V cache: pools [num_pages][Hkv][page_size][D] (bf16 bits),
+    block_table int32 [B][max_pages], seq_lens int32 [B], all CUDA tensors. Returns the status."""
+    return int(load_library().attn_flash_paged_stream(
+        _ptr(Q), _ptr(K_pages), _ptr(V_pages), _ptr(block_table), _ptr(seq_lens), _ptr(O), B, Hq, Hkv, Sq, D,
+        int(causal), page_size, num_pages, max_pages, _ptr(scratch), _stream_handle(stream)))
 
 
 def attn_flash(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_prepacked=0) -> None:

@@ -218,6 +218,39 @@ int attn_flash_stream_out(const uint16_t *Q, const uint16_t *K, const uint16_t *
     return ts_run(&p, scratch, stream);
 }
 
+static int ts_page_size_ok(int ps) {
+    if (ps == 8 || ps == 16 || ps == 32 || ps == 64) return 1;
+    return ps > 0 && ps % ATTN_GPU_KEY_TILE == 0;
+}
+
+int attn_flash_paged_stream(const uint16_t *Q, const uint16_t *K_pages, const uint16_t *V_pages,
+                            const int *block_table, const int *seq_lens, float *O, int B, int Hq, int Hkv, int Sq,
+                            int D, int causal, int page_size, int num_pages, int max_pages, void *scratch,
+                            void *stream) {
+    if (!Q || !K_pages || !V_pages || !block_table || !seq_lens || !O || !scratch) return ATTN_ERR_ARGS;
+    if (B < 1 || Hq < 1 || Hkv < 1 || Hq % Hkv != 0 || Sq < 1 || num_pages < 1 || max_pages < 1)
+        return ATTN_ERR_ARGS;
+    if (D < 8 || D > 128 || D % 8 != 0 || !ts_page_size_ok(page_size)) return ATTN_ERR_ARGS;
+    if ((long long)B * Hq * Sq > 0x7fffffffLL || (long long)max_pages * page_size > 0x7fffffffLL ||
+        (long long)B * max_pages > 0x7fffffffLL)
+        return ATTN_ERR_ARGS;
+    if (((uintptr_t)Q | (uintptr_t)K_pages | (uintptr_t)V_pages | (uintptr_t)O | (uintptr_t)scratch) & 15u)
+        return ATTN_ERR_ALIGN;
+    if (ts_cc_major() != 10) return ATTN_ERR_NOT_SM100;
+    fa_problem p;
+    ts_fill(&p, Q, K_pages, V_pages, B * Hq, B * Hkv, Sq, max_pages * page_size, D, causal, 0);
+    p.O = O;
+    p.paged = 1;
+    p.block_table = block_table;
+    p.seq_lens = seq_lens;
+    p.page_size = page_size;
+    p.max_pages = max_pages;
+    p.num_pages = num_pages;
+    p.hkv_local = Hkv;
+    if (!ts_tc_supported(&p)) return ATTN_ERR_ARGS;
+    return ts_run(&p, scratch, stream);
+}
+
 int attn_flash_partial_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *m, float *l,
                               float *acc, int Hq, int Hkv, int Sq, int Sk_local, int Sk_total, int k_begin, int D,
                               int causal, int bk, void *scratch, int v_prepacked, void *stream) {

@@ -39,6 +39,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "attn_flash.h"
 #include "fa_launch.h"
 #include "sm100_ptx.cuh"
@@ -70,6 +72,11 @@ struct TcParams {
     int snake;    // 1: alternate the direction of the per-CTA item walk every round (causal)
     int group;    // query heads per kv head
     int head_units;  // causal: units per query head when every unit lies within one head, else 0
+    // Paged K/V (paged != 0): K and V are pools [num_pages][hkv_local][page_size][D]; the unit
+    // kv index is b * hkv_local + kv_local for sequence b, whose keys are the pages
+    // block_table[b * max_pages + k / page_size] and whose length is seq_lens[b].
+    const int *block_table, *seq_lens;
+    int paged, page_size, max_pages, num_pages, hkv_local;
     float scale_log2;
 };
 
@@ -111,7 +118,7 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int *s
 // the longest-first list, so the long and short units even out per CTA). Every barrier keeps
 // counting phases across items, so the next item's Q load, first QK and first softmax block
 // overlap the previous item's last PV and epilogue.
-template <int DP, int NQT, bool VT, bool GENERAL>
+template <int DP, int NQT, bool VT, bool GENERAL, bool PAGED>
 __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const TcParams p) {
@@ -152,6 +159,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     //   pieces.
     struct Item {
         int kv, row0, piece, kb0, kb1, nblk;
+        int sk, sk_total;  // keys present (local) and the key axis length the causal rule uses
     };
     auto item_at = [&](int q) {
         Item it;
@@ -181,13 +189,19 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             tile = u % p.tiles_per_kv;
         }
         it.row0 = tile * kBM * NQT;
+        it.sk = p.Sk;
+        it.sk_total = p.Sk_total;
+        if constexpr (PAGED) {  // this sequence's own length, within its block table
+            const int len = __ldg(p.seq_lens + it.kv / p.hkv_local);
+            it.sk = it.sk_total = max(0, min(len, p.Sk));
+        }
         it.kb0 = it.piece < 0 ? 0 : it.piece * p.keys_per_piece;  // local key range [kb0, kb1)
-        it.kb1 = it.piece < 0 ? p.Sk : min(p.Sk, it.kb0 + p.keys_per_piece);
+        it.kb1 = it.piece < 0 ? it.sk : min(it.sk, it.kb0 + p.keys_per_piece);
         int kend = it.kb1;
         if (p.causal) {
             const int rlast = min(it.row0 + kBM * NQT, p.rows_per_kv) - 1;
             const int i_hi = (it.row0 / p.Sq == rlast / p.Sq) ? (rlast % p.Sq) : (p.Sq - 1);
-            const long long lim = (long long)p.Sk_total - p.Sq + i_hi - p.k_begin;  // last live local key
+            const long long lim = (long long)it.sk_total - p.Sq + i_hi - p.k_begin;  // last live local key
             if (lim + 1 < (long long)kend) kend = (int)max(lim + 1, (long long)it.kb0);
         }
         it.nblk = kend > it.kb0 ? (kend - it.kb0 + kBN - 1) / kBN : 0;
@@ -240,6 +254,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
         if (lane == 0) {
             uint32_t gl = 0;   // K/V tile loads issued, over all items
             int qi = 0;        // items with at least one key block, so far
+            int pids[PAGED ? kBN / 8 : 1];  // paged K/V: page ids of the current tile's chunks
             bool ok = true, q_inflight = false;
             for (int r = 0; ok; ++r) {
                 const int q = item_index(r);
@@ -272,6 +287,43 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                     const int key0 = kb0 + (i >> 1) * kBN;
                     const uint32_t dst = sKV + slot * C::KVTILE;
                     const uint32_t bar = kv_full(slot);
+                    if constexpr (PAGED) {
+                        // the tile's keys come from whole pages (page_size <= 128: several pages
+                        // of page_size rows; larger pages: a 128-row part of one page). Page ids
+                        // are read (and checked) for the K tile and reused for the V tile; a
+                        // chunk past the sequence's end reuses a valid page (its keys are masked).
+                        const int P = p.page_size;
+                        const int cs = P < kBN ? P : kBN;
+                        const int nch = kBN / cs;
+                        const int b = kv / p.hkv_local, kvl = kv % p.hkv_local;
+                        if ((i & 1) == 0) {
+                            for (int c = 0; c < nch; ++c) {
+                                const int key = key0 + c * cs;
+                                int pid = c > 0 ? pids[c - 1] : -1;
+                                if (key < it.sk || c == 0) {
+                                    pid = __ldg(p.block_table + (size_t)b * p.max_pages + key / P);
+                                    if (pid < 0 || pid >= p.num_pages) {
+                                        *abort_flag = 1;
+                                        atomicOr(p.status, kDevErrBadPage);
+                                        ok = false;
+                                        break;
+                                    }
+                                }
+                                pids[c] = pid;
+                            }
+                            if (!ok) break;
+                        }
+                        mbar_expect_tx(bar, C::KVTILE);
+                        const CUtensorMap *tm = (i & 1) == 0 ? &tmK : &tmV;
+                        for (int c = 0; c < nch; ++c) {
+                            const int key = key0 + c * cs;
+#pragma unroll
+                            for (int bx = 0; bx < NBOX_D; ++bx)
+                                tma_load_3d(dst + bx * (kBN * 128) + c * cs * 128, tm, bar, bx * 64, key % P,
+                                            pids[c] * p.hkv_local + kvl);
+                        }
+                        continue;
+                    }
                     mbar_expect_tx(bar, C::KVTILE);
                     if ((i & 1) == 0) {
 #pragma unroll
@@ -426,8 +478,9 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
         const int prow = row0 + t * kBM + r;  // packed row within this kv head
         const bool valid = prow < p.rows_per_kv;
         const int ipos = valid ? prow % p.Sq : 0;
-        const long long lim = p.causal ? ((long long)p.Sk_total - p.Sq + ipos - p.k_begin)
-                                       : (long long)(p.Sk - 1);  // last live local key of this row
+        const int sk_total = PAGED ? it.sk_total : p.Sk_total, sk = PAGED ? it.sk : p.Sk;
+        const long long lim = p.causal ? ((long long)sk_total - p.Sq + ipos - p.k_begin)
+                                       : (long long)(sk - 1);  // last live local key of this row
         const long long lastkey = min(lim, (long long)kb1 - 1);
 
         float m = -INFINITY, l = 0.f;
@@ -623,34 +676,41 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 mult = (l > 0.f) ? 1.f / l : 0.f;
                 out_bf16 = p.o_bf16 != 0;
             }
+            auto store_rows = [&](auto bf16_tag) {
+                constexpr bool kBf16 = decltype(bf16_tag)::value;
 #pragma unroll
-            for (int cc = 0; cc < DP / 32; ++cc) {
-                uint32_t o[32];
-                if (have_o) {
-                    tmem_ld32(tO + cc * 32, o);
-                } else {
+                for (int cc = 0; cc < DP / 32; ++cc) {
+                    uint32_t o[32];
+                    if (have_o) {
+                        tmem_ld32(tO + cc * 32, o);
+                    } else {
 #pragma unroll
-                    for (int u = 0; u < 32; ++u) o[u] = 0u;
-                }
-                if (valid) {
+                        for (int u = 0; u < 32; ++u) o[u] = 0u;
+                    }
+                    if (valid) {
 #pragma unroll
-                    for (int v = 0; v < 8; ++v) {
-                        const int c = cc * 32 + 4 * v;
-                        if (c < D) {
-                            float4 w = make_float4(u2f(o[4 * v]) * mult, u2f(o[4 * v + 1]) * mult,
-                                                   u2f(o[4 * v + 2]) * mult, u2f(o[4 * v + 3]) * mult);
-                            if (out_bf16) {
-                                uint16_t *ob = reinterpret_cast<uint16_t *>(p.O) + grow * D + c;
-                                *reinterpret_cast<uint2 *>(ob) =
-                                    make_uint2(f32_to_bf16_bits(w.x) | (f32_to_bf16_bits(w.y) << 16),
-                                               f32_to_bf16_bits(w.z) | (f32_to_bf16_bits(w.w) << 16));
-                            } else {
-                                *reinterpret_cast<float4 *>(dst + c) = w;
+                        for (int v = 0; v < 8; ++v) {
+                            const int c = cc * 32 + 4 * v;
+                            if (c < D) {
+                                float4 w = make_float4(u2f(o[4 * v]) * mult, u2f(o[4 * v + 1]) * mult,
+                                                       u2f(o[4 * v + 2]) * mult, u2f(o[4 * v + 3]) * mult);
+                                if constexpr (kBf16) {
+                                    uint16_t *ob = reinterpret_cast<uint16_t *>(p.O) + grow * D + c;
+                                    *reinterpret_cast<uint2 *>(ob) =
+                                        make_uint2(f32_to_bf16_bits(w.x) | (f32_to_bf16_bits(w.y) << 16),
+                                                   f32_to_bf16_bits(w.z) | (f32_to_bf16_bits(w.w) << 16));
+                                } else {
+                                    *reinterpret_cast<float4 *>(dst + c) = w;
+                                }
                             }
                         }
                     }
                 }
-            }
+            };
+            if (out_bf16)
+                store_rows(std::true_type{});
+            else
+                store_rows(std::false_type{});
         }
         }
         // teardown (softmax warpgroups): TMEM reads done before the dealloc below
@@ -692,11 +752,11 @@ static bool make_map_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t 
     return r == CUDA_SUCCESS;
 }
 
-template <int DP, int NQT, bool VT, bool GENERAL>
+template <int DP, int NQT, bool VT, bool GENERAL, bool PAGED>
 static int launch_tc_inst(cudaStream_t st, const CUtensorMap &tmQ, const CUtensorMap &tmK, const CUtensorMap &tmV,
                           const TcParams &prm, dim3 grid) {
     using C = TcConfig<DP, NQT>;
-    auto kern = fa_tc_kernel<DP, NQT, VT, GENERAL>;
+    auto kern = fa_tc_kernel<DP, NQT, VT, GENERAL, PAGED>;
     static int attr_done[64] = {0};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return ATTN_ERR_CUDA;
@@ -718,12 +778,20 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     const uint64_t D = (uint64_t)P->D;
     CUtensorMap tmQ, tmK, tmV;
     if (!make_map_3d(&tmQ, P->Q, D, rows, P->Hkv, D * 2, rows * D * 2, kBM)) return ATTN_ERR_CUDA;
-    if (!make_map_3d(&tmK, P->K, D, P->Sk, P->Hkv, D * 2, (uint64_t)P->Sk * D * 2, kBN)) return ATTN_ERR_CUDA;
-    if (!VT) {
-        if (!make_map_3d(&tmV, P->V, D, P->Sk, P->Hkv, D * 2, (uint64_t)P->Sk * D * 2, kBN)) return ATTN_ERR_CUDA;
+    if (P->paged) {  // page pools: {D, rows of a page, page x kv head}, boxes of up to 128 rows
+        const uint64_t ps = (uint64_t)P->page_size;
+        const uint32_t box = P->page_size < kBN ? (uint32_t)P->page_size : (uint32_t)kBN;
+        const uint64_t planes = (uint64_t)P->num_pages * P->hkv_local;
+        if (!make_map_3d(&tmK, P->K, D, ps, planes, D * 2, ps * D * 2, box)) return ATTN_ERR_CUDA;
+        if (!make_map_3d(&tmV, P->V, D, ps, planes, D * 2, ps * D * 2, box)) return ATTN_ERR_CUDA;
     } else {
-        if (!make_map_3d(&tmV, P->V, P->Sk, D, P->Hkv, (uint64_t)P->Sk * 2, (uint64_t)P->Sk * D * 2, DP))
+        if (!make_map_3d(&tmK, P->K, D, P->Sk, P->Hkv, D * 2, (uint64_t)P->Sk * D * 2, kBN)) return ATTN_ERR_CUDA;
+        if (!VT) {
+            if (!make_map_3d(&tmV, P->V, D, P->Sk, P->Hkv, D * 2, (uint64_t)P->Sk * D * 2, kBN))
+                return ATTN_ERR_CUDA;
+        } else if (!make_map_3d(&tmV, P->V, P->Sk, D, P->Hkv, (uint64_t)P->Sk * 2, (uint64_t)P->Sk * D * 2, DP)) {
             return ATTN_ERR_CUDA;
+        }
     }
     TcParams prm;
     prm.O = P->O;
@@ -752,18 +820,27 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     prm.part_rows = P->Hq * P->Sq - P->row_base;
     prm.write_partials = P->write_partials;
     prm.o_bf16 = P->o_bf16;
+    prm.block_table = P->block_table;
+    prm.seq_lens = P->seq_lens;
+    prm.paged = P->paged;
+    prm.page_size = P->page_size;
+    prm.max_pages = P->max_pages;
+    prm.num_pages = P->num_pages;
+    prm.hkv_local = P->hkv_local > 0 ? P->hkv_local : 1;
     prm.scale_log2 = P->scale_log2;
     prm.group = group;
     prm.head_units = (P->Sq % (kBM * NQT) == 0) ? P->Sq / (kBM * NQT) : 0;
     const int sms = ts_num_sms() > 0 ? ts_num_sms() : 1;
-    if (prm.n_direct == units && !prm.write_partials) {
+    if (prm.n_direct == units && !prm.write_partials && !P->paged) {
         prm.n_items = units;
         prm.snake = prm.causal;
-        return launch_tc_inst<DP, NQT, VT, false>(st, tmQ, tmK, tmV, prm, dim3(min(units, sms)));
+        return launch_tc_inst<DP, NQT, VT, false, false>(st, tmQ, tmK, tmV, prm, dim3(min(units, sms)));
     }
     prm.n_items = prm.n_direct + (units - prm.n_direct) * prm.pieces;
     prm.snake = 0;
-    return launch_tc_inst<DP, NQT, VT, true>(st, tmQ, tmK, tmV, prm, dim3(min(prm.n_items, sms)));
+    if (P->paged)  // paged K/V: the general work plan, V row-major
+        return launch_tc_inst<DP, NQT, false, true, true>(st, tmQ, tmK, tmV, prm, dim3(min(prm.n_items, sms)));
+    return launch_tc_inst<DP, NQT, VT, true, false>(st, tmQ, tmK, tmV, prm, dim3(min(prm.n_items, sms)));
 }
 
 static int nqt_for(const fa_problem *P) {

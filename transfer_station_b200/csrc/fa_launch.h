@@ -40,6 +40,12 @@ typedef struct fa_problem {
      * half full splits only that wave's units. */
     int n_direct;
     int row_base;
+    /* Paged K/V (paged != 0, tensor-core path only): K and V are pools
+     * [num_pages][hkv_local][page_size][D]; kv head index = b * hkv_local + kv_local for
+     * sequence b, whose keys live in pages block_table[b * max_pages + k / page_size] and whose
+     * length is seq_lens[b] (device arrays); Sk is the bound max_pages * page_size. */
+    const int *block_table, *seq_lens;
+    int paged, page_size, max_pages, num_pages, hkv_local;
     float scale_log2;          /* (1/sqrt(D)) * log2(e) */
 } fa_problem;
 

@@ -20,6 +20,7 @@ enum : int {
     kDevErrTimeoutS = 1 << 2,      // softmax waited too long for a score tile
     kDevErrTimeoutP = 1 << 3,      // MMA waited too long for a P tile
     kDevErrTimeoutDrain = 1 << 4,  // teardown waited too long for in-flight copies / MMAs
+    kDevErrBadPage = 1 << 5,       // a paged K/V block table held a page id outside the pool
 };
 
 // ~2 s: every wait in these kernels is on a producer inside the same CTA, which completes
