@@ -19,7 +19,8 @@ Keys of the JSON line beyond the base contract:
                 Q, K, V host->device and O device->host inside the timed region; two CUDA
                 streams take alternate steps, so one step's readback overlaps the next upload
   decode        a secondary HBM-bound line: BASELINE config 3 (GQA decode, B=64, Sk=8192), per GPU
-  long_decode   BASELINE config 5 decode (B=4, Hq=64, Hkv=8, Sk=131072) with the key axis split
+  paged_decode  the same decode through attn_flash_paged_stream (64-key pages, shuffled table)
+  long_decode  BASELINE config 5 decode (B=4, Hq=64, Hkv=8, Sk=131072) with the key axis split
                 over all ranks: partial attention per rank, one NCCL all-gather of the (m, l, acc)
                 partials, merge on every rank (transfer_station_b200.multigpu)
   gpu_launches  kernels the library launched inside the timed region (its own counter)
@@ -436,6 +437,48 @@ def run_ours(args, w) -> None:
                        "l2": "K+V = 2 GiB per step > L2"}
         del tq, tk, tv, to
 
+    # ---------------- the same decode through the paged K/V entry point (64-key pages, shuffled)
+    paged_line = None
+    if not args.no_decode and not decode:
+        pB, pHq, pHkv, pSk, pD, pP = 64, 32, 8, 8192, 128, 64
+        npages = pB * pSk // pP
+        g = torch.Generator(device=dev)
+        g.manual_seed(2)
+        pq = torch.randn(pB * pHq * pD, device=dev, generator=g).to(torch.bfloat16).view(torch.int16)
+        pk = torch.randn(npages * pHkv * pP * pD, device=dev, generator=g).to(torch.bfloat16).view(torch.int16)
+        pv = torch.randn(npages * pHkv * pP * pD, device=dev, generator=g).to(torch.bfloat16).view(torch.int16)
+        table = torch.randperm(npages, device=dev, generator=g).to(torch.int32)
+        lens = torch.full((pB,), pSk, dtype=torch.int32, device=dev)
+        po = torch.empty(pB * pHq * pD, dtype=torch.float32, device=dev)
+
+        def paged_step():
+            rc = ts.attn_flash_paged_stream(pq, pk, pv, table, lens, po, pB, pHq, pHkv, 1, pD, 0, pP, npages,
+                                            pSk // pP, scratch, stream)
+            if rc != ts.ATTN_OK:
+                raise ts.AttnError(rc, "attn_flash_paged_stream")
+
+        psteps = max(3, min(args.steps, 200))
+        for _ in range(3):
+            paged_step()
+        barrier()
+        e0.record(stream)
+        for _ in range(psteps):
+            paged_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        pms = max_over_ranks(e0.elapsed_time(e1)) / psteps
+        rc, code = ts.attn_flash_status(scratch, stream)
+        if rc != ts.ATTN_OK:
+            raise ts.AttnError(rc, f"paged decode device status {code}")
+        pby = algo_bytes(pB * pHq, pB * pHkv, 1, pSk, pD)
+        pach = pby / (pms / 1e3) / 1e9
+        paged_line = {"workload": "gqa_decode_b64_sk8192_paged64",
+                      "desc": "BASELINE config 3 shape through attn_flash_paged_stream: 64-key pages in a "
+                              "shuffled block table", "value": world * pach, "unit": "GB/s", "per_gpu_gbs": pach,
+                      "ms_per_step": pms, "frac_of_measured_hbm": pach / peaks["hbm_gbs"], "steps": psteps}
+        del pq, pk, pv, table, lens, po
+
     # ---------------- long-context decode, key axis split over the ranks (NCCL merge)
     long_line = None
     if not args.no_decode:
@@ -500,6 +543,7 @@ def run_ours(args, w) -> None:
             "gpu_launches": int(launches),
             "clocks": csum,
             "decode": decode_line,
+            "paged_decode": paged_line,
             "long_decode": long_line,
         }
         print(json.dumps(line), flush=True)

@@ -87,7 +87,8 @@ struct TcConfig {
     static constexpr int NS_RAW = (kSmemBudget - NQT * QTILE) / KVTILE;
     static constexpr int NS = NS_RAW > 8 ? 8 : NS_RAW;  // K/V ring slots
     static constexpr int NBAR = 3 + 2 * NS + 3 * NQT;   // q_full/empty, done, kv_full/empty, s/p/o_full
-    static constexpr int SMEM = 1024 + NQT * QTILE + NS * KVTILE + NBAR * 8 + 16;
+    static constexpr int PID_WIN = 512;  // paged K/V: page ids staged in shared memory at a time
+    static constexpr int SMEM = 1024 + NQT * QTILE + NS * KVTILE + NBAR * 8 + 16 + PID_WIN * 4;
     static constexpr int THREADS = 128 + 128 * NQT;
     static constexpr uint32_t TMEM_COLS = (NQT * kBN + NQT * DP) <= 256 ? 256u : 512u;
     static_assert(NS >= 2, "K/V ring needs at least two slots");
@@ -145,6 +146,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     auto o_full = [&](int t) { return bar0 + 24 + 8u * (2 * NS + 2 * NQT + t); }; // an item's O_t final
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + (bar0 - base_u32) + C::NBAR * 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    int *pid_win = reinterpret_cast<int *>(tmem_slot + 4);  // paged K/V: C::PID_WIN page ids
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -249,12 +251,115 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     // 128 x 128 + 256 x 184 = 63488 <= 384 x 168 = 64512 (neither side spills).
     if (warp < 4) {
         if constexpr (NQT == 2) regs_dec<128>();
-    if (warp == 0) {
+    if (warp == 0 && PAGED) {
+        // ============================ TMA producer, paged K/V (the whole warp)
+        // The warp stages C::PID_WIN page ids of the item at a time in shared memory (checking
+        // each id of a page that holds live keys against the pool; ids of pages past the
+        // sequence's end are never read), then lane 0 issues each tile's loads from there: a
+        // 128-key tile is 128 / page_size boxes of page_size rows (page_size <= 128) or a
+        // 128-row part of one page; the 128-byte swizzle repeats every 8 rows, so the boxes
+        // land where one 128-row box would. A chunk past the end reuses the tile's first page
+        // (its keys are masked).
+        const int P = p.page_size;
+        const int cs = P < kBN ? P : kBN;
+        const int nch = kBN / cs;
+        uint32_t gl = 0;
+        int qi = 0;
+        bool ok = true, q_inflight = false;
+        for (int r = 0; ok; ++r) {
+            const int q = item_index(r);
+            if (q >= p.n_items) break;
+            const Item it = item_at(q);
+            if (it.nblk == 0) continue;
+            const int kv = it.kv, kb0 = it.kb0;
+            const int b = kv / p.hkv_local, kvl = kv % p.hkv_local;
+            const int used = (it.sk + P - 1) / P;  // pages that hold this sequence's keys
+            const int *row = p.block_table + (size_t)b * p.max_pages;
+            if (lane == 0) {
+                if (qi > 0 && !mbar_wait(q_empty, (qi - 1) & 1, abort_flag, p.status, kDevErrTimeoutQ)) ok = false;
+                if (ok) {
+                    mbar_expect_tx(q_full, NQT * C::QTILE);
+#pragma unroll
+                    for (int t = 0; t < NQT; ++t)
+#pragma unroll
+                        for (int bx = 0; bx < NBOX_D; ++bx)
+                            tma_load_3d(sQ + t * C::QTILE + bx * BOX_ROWS128, &tmQ, q_full, bx * 64,
+                                        it.row0 + t * kBM, kv);
+                    q_inflight = true;
+                }
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            int win_base = -1;
+            const int nload = 2 * it.nblk;
+            for (int i = 0; i < nload; ++i, ++gl) {
+                const int key0 = kb0 + (i >> 1) * kBN;
+                const int pg_lo = key0 / P, pg_hi = (key0 + kBN - 1) / P;
+                if (win_base < 0 || pg_hi >= win_base + C::PID_WIN) {  // warp-uniform
+                    win_base = pg_lo;
+                    bool bad = false;
+                    for (int e = lane; e < C::PID_WIN; e += 32) {
+                        const int pg = win_base + e;
+                        int id = -1;
+                        if (pg < used && pg < p.max_pages) {
+                            id = __ldg(row + pg);
+                            if (id < 0 || id >= p.num_pages) bad = true;
+                        }
+                        pid_win[e] = id;
+                    }
+                    bad = __any_sync(0xffffffffu, bad);
+                    __syncwarp();
+                    if (bad) {
+                        if (lane == 0) {
+                            *abort_flag = 1;
+                            atomicOr(p.status, kDevErrBadPage);
+                        }
+                        ok = false;
+                        break;
+                    }
+                }
+                const int slot = gl % NS;
+                const int round = gl / NS;
+                const uint32_t bar = kv_full(slot);
+                if (lane == 0) {
+                    if (round > 0 &&
+                        !mbar_wait(kv_empty(slot), (round - 1) & 1, abort_flag, p.status, kDevErrTimeoutKV))
+                        ok = false;
+                    else
+                        mbar_expect_tx(bar, C::KVTILE);  // armed before any lane's copy can land
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;  // gl counts the loads issued so far
+                // lane c issues chunk c's boxes, so a tile of many small pages goes out in parallel
+                const uint32_t dst = sKV + slot * C::KVTILE;
+                const CUtensorMap *tm = (i & 1) == 0 ? &tmK : &tmV;
+                for (int c = lane; c < nch; c += 32) {
+                    const int key = key0 + c * cs;
+                    int id = pid_win[key / P - win_base];
+                    if (id < 0) id = pid_win[pg_lo - win_base];
+#pragma unroll
+                    for (int bx = 0; bx < NBOX_D; ++bx)
+                        tma_load_3d(dst + bx * (kBN * 128) + c * cs * 128, tm, bar, bx * 64, key % P,
+                                    id * p.hkv_local + kvl);
+                }
+                __syncwarp();
+            }
+            if (ok) {
+                q_inflight = false;
+                ++qi;
+            }
+        }
+        if (!ok && lane == 0) {  // let the copies already in flight land before the CTA exits
+            if (q_inflight) drain_wait(q_full, qi & 1, p.status);
+            for (uint32_t i = gl > (uint32_t)NS ? gl - NS : 0u; i < gl; ++i)
+                drain_wait(kv_full(i % NS), (i / NS) & 1, p.status);
+        }
+        __syncwarp();
+    } else if (warp == 0) {
         // ============================ TMA producer
         if (lane == 0) {
             uint32_t gl = 0;   // K/V tile loads issued, over all items
             int qi = 0;        // items with at least one key block, so far
-            int pids[PAGED ? kBN / 8 : 1];  // paged K/V: page ids of the current tile's chunks
             bool ok = true, q_inflight = false;
             for (int r = 0; ok; ++r) {
                 const int q = item_index(r);
@@ -287,43 +392,6 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                     const int key0 = kb0 + (i >> 1) * kBN;
                     const uint32_t dst = sKV + slot * C::KVTILE;
                     const uint32_t bar = kv_full(slot);
-                    if constexpr (PAGED) {
-                        // the tile's keys come from whole pages (page_size <= 128: several pages
-                        // of page_size rows; larger pages: a 128-row part of one page). Page ids
-                        // are read (and checked) for the K tile and reused for the V tile; a
-                        // chunk past the sequence's end reuses a valid page (its keys are masked).
-                        const int P = p.page_size;
-                        const int cs = P < kBN ? P : kBN;
-                        const int nch = kBN / cs;
-                        const int b = kv / p.hkv_local, kvl = kv % p.hkv_local;
-                        if ((i & 1) == 0) {
-                            for (int c = 0; c < nch; ++c) {
-                                const int key = key0 + c * cs;
-                                int pid = c > 0 ? pids[c - 1] : -1;
-                                if (key < it.sk || c == 0) {
-                                    pid = __ldg(p.block_table + (size_t)b * p.max_pages + key / P);
-                                    if (pid < 0 || pid >= p.num_pages) {
-                                        *abort_flag = 1;
-                                        atomicOr(p.status, kDevErrBadPage);
-                                        ok = false;
-                                        break;
-                                    }
-                                }
-                                pids[c] = pid;
-                            }
-                            if (!ok) break;
-                        }
-                        mbar_expect_tx(bar, C::KVTILE);
-                        const CUtensorMap *tm = (i & 1) == 0 ? &tmK : &tmV;
-                        for (int c = 0; c < nch; ++c) {
-                            const int key = key0 + c * cs;
-#pragma unroll
-                            for (int bx = 0; bx < NBOX_D; ++bx)
-                                tma_load_3d(dst + bx * (kBN * 128) + c * cs * 128, tm, bar, bx * 64, key % P,
-                                            pids[c] * p.hkv_local + kvl);
-                        }
-                        continue;
-                    }
                     mbar_expect_tx(bar, C::KVTILE);
                     if ((i & 1) == 0) {
 #pragma unroll
