@@ -192,6 +192,52 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict
     }
 }
 
+// Few parts (2..4: a prefill's last-wave split, most decode splits), normalised output: one
+// thread per (row, 4 columns). A thread's loads -- every part's m, l and its 4 columns of acc --
+// do not depend on one another, so they are all in flight at once (one memory round trip
+// instead of reduce-then-load); the m and l loads of a warp's 32 lanes hit one address each.
+template <int NP>
+__global__ void __launch_bounds__(256) fa_combine_few(const float *__restrict__ m, const float *__restrict__ l,
+                                                      const float *__restrict__ acc, int rows, int D,
+                                                      float *__restrict__ out, int out_bf16) {
+    const int cpr = D >> 2;  // float4 chunks per row (D % 4 == 0)
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long r = idx / cpr;
+    if (r >= rows) return;
+    const int c = (int)(idx - r * cpr) * 4;
+    float ms[NP], ls[NP];
+    float4 a[NP];
+#pragma unroll
+    for (int s = 0; s < NP; ++s) {
+        const size_t sr = (size_t)s * rows + r;
+        ms[s] = m[sr];
+        ls[s] = l[sr];
+        a[s] = *reinterpret_cast<const float4 *>(acc + sr * D + c);
+    }
+    float mx = ms[0];
+#pragma unroll
+    for (int s = 1; s < NP; ++s) mx = fmaxf(mx, ms[s]);
+    float L = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < NP; ++s) {
+        const float w = (ms[s] != -INFINITY) ? ex2f(ms[s] - mx) : 0.f;
+        L = fmaf(w, ls[s], L);
+        o.x = fmaf(w, a[s].x, o.x);
+        o.y = fmaf(w, a[s].y, o.y);
+        o.z = fmaf(w, a[s].z, o.z);
+        o.w = fmaf(w, a[s].w, o.w);
+    }
+    const float inv = (L > 0.f) ? 1.f / L : 0.f;
+    o = make_float4(o.x * inv, o.y * inv, o.z * inv, o.w * inv);
+    if (out_bf16)
+        *reinterpret_cast<uint2 *>(reinterpret_cast<uint16_t *>(out) + (size_t)r * D + c) =
+            make_uint2(f32_to_bf16_bits(o.x) | (f32_to_bf16_bits(o.y) << 16),
+                       f32_to_bf16_bits(o.z) | (f32_to_bf16_bits(o.w) << 16));
+    else
+        *reinterpret_cast<float4 *>(out + (size_t)r * D + c) = o;
+}
+
 }  // namespace ts
 
 extern "C" int ts_num_sms(void) {
@@ -222,6 +268,20 @@ extern "C" int ts_launch_combine(const float *m, const float *l, const float *ac
     const int warps = 8;
     dim3 grid((rows + warps - 1) / warps);
     const bool vec = (D % 4 == 0) && ((((uintptr_t)acc) | ((uintptr_t)O)) & 15u) == 0;
+    if (vec && !out_m && nparts >= 2 && nparts <= 4) {
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        const long long threads = (long long)rows * (D / 4);
+        const dim3 g((unsigned)((threads + 255) / 256));
+        if (nparts == 2)
+            ts::fa_combine_few<2><<<g, 256, 0, st>>>(m, l, acc, rows, D, O, out_bf16);
+        else if (nparts == 3)
+            ts::fa_combine_few<3><<<g, 256, 0, st>>>(m, l, acc, rows, D, O, out_bf16);
+        else
+            ts::fa_combine_few<4><<<g, 256, 0, st>>>(m, l, acc, rows, D, O, out_bf16);
+        if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
+        ts_count_launch();
+        return ATTN_OK;
+    }
     if (vec)
         ts::fa_combine_kernel<true><<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows,
                                                                                                D, O, out_m, out_l,
