@@ -21,8 +21,8 @@ Keys of the JSON line beyond the base contract:
   decode        a secondary HBM-bound line: BASELINE config 3 (GQA decode, B=64, Sk=8192), per GPU
   paged_decode  the same decode through attn_flash_paged_stream (64-key pages, shuffled table)
   long_decode  BASELINE config 5 decode (B=4, Hq=64, Hkv=8, Sk=131072) with the key axis split
-                over all ranks: partial attention per rank, one NCCL all-gather of the (m, l, acc)
-                partials, merge on every rank (transfer_station_b200.multigpu)
+                over all ranks: partial attention per rank into one packed (m, l, acc) block, one
+                NCCL all-gather of the blocks, merge on every rank (transfer_station_b200.multigpu)
   gpu_launches  kernels the library launched inside the timed region (its own counter)
   clocks        SM clocks / throttle reasons sampled by NVML during the timed region
 
@@ -513,7 +513,7 @@ def run_ours(args, w) -> None:
                      "per_gpu_gbs": lby / (lms / 1e3) / 1e9 / world, "ms_per_step": lms,
                      "frac_of_measured_hbm_per_gpu": lby / (lms / 1e3) / 1e9 / world / peaks["hbm_gbs"],
                      "bytes_per_step": lby, "steps": lsteps, "scaling": "strong (key axis split over ranks)",
-                     "merge": "one NCCL all-gather each of m, l [B*Hq] and acc [B*Hq, D] fp32, then combine"}
+                     "merge": "one NCCL all-gather of packed (m, l, acc) fp32 blocks, then combine"}
         del lq, lk, lv, lo
 
     # ---------------- CPU baseline (rank 0, N=1 only)

@@ -160,6 +160,18 @@ int attn_flash_partial_stream(const uint16_t *Q, const uint16_t *K, const uint16
 int attn_flash_combine_stream(const float *m, const float *l, const float *acc, int nparts,
                               int rows, int D, float *O, void *stream);
 
+/* Floats of one packed partial: m [rows], l [rows], padding to a multiple of 4 floats, then
+ * acc [rows][D]. A rank of a key-split decode lets attn_flash_partial_stream write its m, l and
+ * acc into one such block, so one all-gather moves every rank's partials together. No
+ * counterpart in the reference (one call on one core). */
+size_t attn_flash_packed_floats(int rows, int D);
+
+/* attn_flash_combine_stream over nparts packed partials laid out back to back:
+ * parts[s * attn_flash_packed_floats(rows, D) + ...] (what one all-gather of the per-rank
+ * blocks produces). */
+int attn_flash_combine_packed_stream(const float *parts, int nparts, int rows, int D, float *O,
+                                     void *stream);
+
 /* attn_flash without a scratch argument, for callers that cannot allocate device memory (a
  * host whose device memory belongs to its own pool allocator, or a foreign-function binding
  * with nowhere to keep a device buffer between calls). No counterpart in the reference: its

@@ -78,3 +78,36 @@ def test_partial_of_whole_range_equals_attention(cuda_dev):
     rows = np.arange(Sq, dtype=np.int32)
     ref = oracle.attn_ref(Q, K, V, Hq, Hkv, Sq, Sk, D, 0, rows)
     assert oracle.passes(oracle.cmp_rows(ref, out, Hq, Sq, D, rows))
+
+
+@pytest.mark.parametrize("nparts", [1, 2, 3, 4, 5])
+@pytest.mark.parametrize("rows,D", [(9, 64), (17, 70), (512, 128)])
+def test_packed_combine_equals_separate(cuda_dev, nparts, rows, D):
+    """attn_flash_combine_packed_stream over back-to-back packed blocks (what one all-gather of
+    the ranks' blocks yields) gives the same bits as attn_flash_combine_stream over separate
+    m, l, acc arrays: odd row counts exercise the padding before acc, D=70 the unvectorised
+    kernel, and a part with m = -inf (an empty key shard) must contribute nothing."""
+    g = torch.Generator().manual_seed(rows * 31 + nparts)
+    m = torch.randn(nparts, rows, generator=g) * 4
+    l = torch.rand(nparts, rows, generator=g) * 50 + 1
+    acc = torch.randn(nparts, rows, D, generator=g)
+    if nparts > 1:
+        m[-1, ::3] = float("-inf")
+        l[-1, ::3] = 0
+        acc[-1, ::3] = 0
+    stride = ts.attn_flash_packed_floats(rows, D)
+    off = -(-2 * rows // 4) * 4
+    assert stride == off + rows * D
+    packed = torch.zeros(nparts, stride)
+    packed[:, :rows] = m
+    packed[:, rows:2 * rows] = l
+    packed[:, off:] = acc.reshape(nparts, -1)
+    md, ld, ad, pd = (t.contiguous().to(cuda_dev) for t in (m, l, acc, packed))
+    o1 = torch.empty(rows * D, dtype=torch.float32, device=cuda_dev)
+    o2 = torch.empty_like(o1)
+    assert ts.attn_flash_combine_stream(md, ld, ad, nparts, rows, D, o1) == ts.ATTN_OK
+    assert ts.attn_flash_combine_packed_stream(pd, nparts, rows, D, o2) == ts.ATTN_OK
+    torch.cuda.synchronize()
+    assert torch.equal(o1.view(torch.int32), o2.view(torch.int32))
+    ref = oracle.combine(m.numpy(), l.numpy(), acc.numpy(), nparts, rows, D)  # m in the log2 domain
+    assert np.allclose(o2.cpu().numpy(), ref, rtol=1e-5, atol=1e-6)

@@ -64,9 +64,18 @@ def _worker(rank, world, port, case, out_path):
         Ks = np.ascontiguousarray(K.reshape(Hkv, Sk, D)[:, k0:k0 + kl]).reshape(-1)
         Vs = np.ascontiguousarray(V.reshape(Hkv, Sk, D)[:, k0:k0 + kl]).reshape(-1)
         m, l, acc = np_partial(Q, Ks, Vs, Hq, Hkv, Sq, Sk, k0, kl, D, causal)
-        all_m, all_l, all_acc = multigpu.gather_partials(torch.from_numpy(m), torch.from_numpy(l),
-                                                         torch.from_numpy(acc))
-        O = oracle.combine(all_m.numpy(), all_l.numpy(), all_acc.numpy(), world, Hq * Sq, D)
+        rows = Hq * Sq
+        buf = torch.zeros(multigpu.packed_floats(rows, D), dtype=torch.float32)
+        pm, pl, pacc = multigpu.packed_views(buf, rows, D)
+        pm.copy_(torch.from_numpy(m))
+        pl.copy_(torch.from_numpy(l))
+        pacc.copy_(torch.from_numpy(acc))
+        parts = multigpu.gather_packed(buf).view(world, -1)  # one collective for all three
+        views = [multigpu.packed_views(parts[r], rows, D) for r in range(world)]
+        all_m = np.stack([v[0].numpy() for v in views])
+        all_l = np.stack([v[1].numpy() for v in views])
+        all_acc = np.stack([v[2].numpy() for v in views])
+        O = oracle.combine(all_m, all_l, all_acc, world, rows, D)
         if rank == 0:
             np.save(out_path, O)
     finally:

@@ -55,6 +55,9 @@ EXPORTS = {
                                   [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "attn_flash_combine_stream": (ctypes.c_int, [_f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                  _f32p, ctypes.c_void_p]),
+    "attn_flash_packed_floats": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    "attn_flash_combine_packed_stream": (ctypes.c_int, [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p,
+                                                        ctypes.c_void_p]),
     "attn_flash_noalloc": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 8 + [ctypes.c_void_p]),
 }
 
@@ -141,6 +144,17 @@ def attn_flash_paged_stream(Q, K_pages, V_pages, block_table, seq_lens, O, B, Hq
     return int(load_library().attn_flash_paged_stream(
         _ptr(Q), _ptr(K_pages), _ptr(V_pages), _ptr(block_table), _ptr(seq_lens), _ptr(O), B, Hq, Hkv, Sq, D,
         int(causal), page_size, num_pages, max_pages, _ptr(scratch), _stream_handle(stream)))
+
+
+def attn_flash_packed_floats(rows: int, D: int) -> int:
+    """Floats of one packed partial block (m, l, padding, acc)."""
+    return int(load_library().attn_flash_packed_floats(rows, D))
+
+
+def attn_flash_combine_packed_stream(parts, nparts, rows, D, O, stream=None) -> int:
+    """Merge nparts packed partial blocks laid out back to back into O [rows][D] fp32."""
+    return int(load_library().attn_flash_combine_packed_stream(_ptr(parts), nparts, rows, D, _ptr(O),
+                                                                _stream_handle(stream)))
 
 
 def attn_flash(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_prepacked=0) -> None:

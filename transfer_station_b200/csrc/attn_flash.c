@@ -276,6 +276,20 @@ int attn_flash_combine_stream(const float *m, const float *l, const float *acc, 
     return ts_launch_combine(m, l, acc, nparts, rows, D, O, NULL, NULL, 0, stream);
 }
 
+size_t attn_flash_packed_floats(int rows, int D) {
+    if (rows < 0 || D < 1) return 0;
+    return ((2 * (size_t)rows + 3) & ~(size_t)3) + (size_t)rows * D;
+}
+
+int attn_flash_combine_packed_stream(const float *parts, int nparts, int rows, int D, float *O, void *stream) {
+    if (!parts || !O || nparts < 1 || rows < 0 || D < 1 || D > ATTN_D_MAX) return ATTN_ERR_ARGS;
+    if (ts_cc_major() != 10) return ATTN_ERR_NOT_SM100;
+    const size_t ml = (2 * (size_t)rows + 3) & ~(size_t)3;
+    const size_t stride = attn_flash_packed_floats(rows, D);
+    return ts_launch_combine_strided(parts, parts + rows, parts + ml, nparts, rows, D, stride, stride, O, NULL, NULL,
+                                     0, stream);
+}
+
 int attn_flash_status(void *scratch, void *stream, int *device_code) {
     if (!scratch) return ATTN_ERR_ARGS;
     ts_scratch s;

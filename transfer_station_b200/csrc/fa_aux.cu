@@ -133,19 +133,20 @@ __global__ void __launch_bounds__(256) fa_simt_kernel(const SimtParams p) {
 template <bool VEC>
 __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict__ m, const float *__restrict__ l,
                                                          const float *__restrict__ acc, int nparts, int rows, int D,
-                                                         float *__restrict__ out, float *__restrict__ out_m,
-                                                         float *__restrict__ out_l, int out_bf16) {
+                                                         size_t ps_ml, size_t ps_acc, float *__restrict__ out,
+                                                         float *__restrict__ out_m, float *__restrict__ out_l,
+                                                         int out_bf16) {
     const int lane = threadIdx.x & 31;
     const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= rows) return;
     float mx = -INFINITY;
-    for (int s = lane; s < nparts; s += 32) mx = fmaxf(mx, m[(size_t)s * rows + r]);
+    for (int s = lane; s < nparts; s += 32) mx = fmaxf(mx, m[(size_t)s * ps_ml + r]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float L = 0.f;
     for (int s = lane; s < nparts; s += 32) {
-        const float ms = m[(size_t)s * rows + r];
-        if (ms != -INFINITY) L = fmaf(ex2f(ms - mx), l[(size_t)s * rows + r], L);
+        const float ms = m[(size_t)s * ps_ml + r];
+        if (ms != -INFINITY) L = fmaf(ex2f(ms - mx), l[(size_t)s * ps_ml + r], L);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
@@ -155,9 +156,9 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict
             float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
             for (int s = 0; s < nparts; ++s) {
-                const float ms = m[(size_t)s * rows + r];
+                const float ms = m[(size_t)s * ps_ml + r];
                 const float w = (ms != -INFINITY) ? ex2f(ms - mx) : 0.f;
-                const float4 x = *reinterpret_cast<const float4 *>(acc + ((size_t)s * rows + r) * D + c);
+                const float4 x = *reinterpret_cast<const float4 *>(acc + (size_t)s * ps_acc + (size_t)r * D + c);
                 a.x = fmaf(w, x.x, a.x);
                 a.y = fmaf(w, x.y, a.y);
                 a.z = fmaf(w, x.z, a.z);
@@ -176,9 +177,9 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict
             float a = 0.f;
 #pragma unroll 4
             for (int s = 0; s < nparts; ++s) {
-                const float ms = m[(size_t)s * rows + r];
+                const float ms = m[(size_t)s * ps_ml + r];
                 const float w = (ms != -INFINITY) ? ex2f(ms - mx) : 0.f;
-                a = fmaf(w, acc[((size_t)s * rows + r) * D + c], a);
+                a = fmaf(w, acc[(size_t)s * ps_acc + (size_t)r * D + c], a);
             }
             if (out_bf16)
                 reinterpret_cast<uint16_t *>(out)[(size_t)r * D + c] = (uint16_t)f32_to_bf16_bits(a * inv);
@@ -198,8 +199,8 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict
 // instead of reduce-then-load); the m and l loads of a warp's 32 lanes hit one address each.
 template <int NP>
 __global__ void __launch_bounds__(256) fa_combine_few(const float *__restrict__ m, const float *__restrict__ l,
-                                                      const float *__restrict__ acc, int rows, int D,
-                                                      float *__restrict__ out, int out_bf16) {
+                                                      const float *__restrict__ acc, int rows, int D, size_t ps_ml,
+                                                      size_t ps_acc, float *__restrict__ out, int out_bf16) {
     const int cpr = D >> 2;  // float4 chunks per row (D % 4 == 0)
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long r = idx / cpr;
@@ -209,10 +210,9 @@ __global__ void __launch_bounds__(256) fa_combine_few(const float *__restrict__ 
     float4 a[NP];
 #pragma unroll
     for (int s = 0; s < NP; ++s) {
-        const size_t sr = (size_t)s * rows + r;
-        ms[s] = m[sr];
-        ls[s] = l[sr];
-        a[s] = *reinterpret_cast<const float4 *>(acc + sr * D + c);
+        ms[s] = m[(size_t)s * ps_ml + r];
+        ls[s] = l[(size_t)s * ps_ml + r];
+        a[s] = *reinterpret_cast<const float4 *>(acc + (size_t)s * ps_acc + (size_t)r * D + c);
     }
     float mx = ms[0];
 #pragma unroll
@@ -262,37 +262,44 @@ extern "C" int ts_cc_major(void) {
     return v;
 }
 
-extern "C" int ts_launch_combine(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
-                                 float *O, float *out_m, float *out_l, int out_bf16, void *stream) {
+extern "C" int ts_launch_combine_strided(const float *m, const float *l, const float *acc, int nparts, int rows,
+                                         int D, size_t ps_ml, size_t ps_acc, float *O, float *out_m, float *out_l,
+                                         int out_bf16, void *stream) {
     if (rows <= 0) return ATTN_OK;
     const int warps = 8;
     dim3 grid((rows + warps - 1) / warps);
-    const bool vec = (D % 4 == 0) && ((((uintptr_t)acc) | ((uintptr_t)O)) & 15u) == 0;
+    const bool vec = (D % 4 == 0) && (ps_acc % 4 == 0) && ((((uintptr_t)acc) | ((uintptr_t)O)) & 15u) == 0;
     if (vec && !out_m && nparts >= 2 && nparts <= 4) {
         cudaStream_t st = static_cast<cudaStream_t>(stream);
         const long long threads = (long long)rows * (D / 4);
         const dim3 g((unsigned)((threads + 255) / 256));
         if (nparts == 2)
-            ts::fa_combine_few<2><<<g, 256, 0, st>>>(m, l, acc, rows, D, O, out_bf16);
+            ts::fa_combine_few<2><<<g, 256, 0, st>>>(m, l, acc, rows, D, ps_ml, ps_acc, O, out_bf16);
         else if (nparts == 3)
-            ts::fa_combine_few<3><<<g, 256, 0, st>>>(m, l, acc, rows, D, O, out_bf16);
+            ts::fa_combine_few<3><<<g, 256, 0, st>>>(m, l, acc, rows, D, ps_ml, ps_acc, O, out_bf16);
         else
-            ts::fa_combine_few<4><<<g, 256, 0, st>>>(m, l, acc, rows, D, O, out_bf16);
+            ts::fa_combine_few<4><<<g, 256, 0, st>>>(m, l, acc, rows, D, ps_ml, ps_acc, O, out_bf16);
         if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
         ts_count_launch();
         return ATTN_OK;
     }
     if (vec)
         ts::fa_combine_kernel<true><<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows,
-                                                                                               D, O, out_m, out_l,
-                                                                                               out_bf16);
+                                                                                               D, ps_ml, ps_acc, O,
+                                                                                               out_m, out_l, out_bf16);
     else
         ts::fa_combine_kernel<false><<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows,
-                                                                                                D, O, out_m, out_l,
-                                                                                                out_bf16);
+                                                                                                D, ps_ml, ps_acc, O,
+                                                                                                out_m, out_l, out_bf16);
     if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
     ts_count_launch();
     return ATTN_OK;
+}
+
+extern "C" int ts_launch_combine(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
+                                 float *O, float *out_m, float *out_l, int out_bf16, void *stream) {
+    return ts_launch_combine_strided(m, l, acc, nparts, rows, D, (size_t)rows, (size_t)rows * D, O, out_m, out_l,
+                                     out_bf16, stream);
 }
 
 static int launch_simt(const fa_problem *P, void *stream, int partial) {

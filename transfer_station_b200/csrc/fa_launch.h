@@ -68,6 +68,12 @@ int ts_launch_attention(const fa_problem *p, void *stream);
 int ts_launch_combine(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
                       float *O, float *out_m, float *out_l, int out_bf16, void *stream);
 
+/* The same with each part's m/l and acc `ps_ml` / `ps_acc` floats apart (m[s*ps_ml + r],
+ * acc[s*ps_acc + r*D + c]): packed per-rank partials gathered by one collective. */
+int ts_launch_combine_strided(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
+                              size_t ps_ml, size_t ps_acc, float *O, float *out_m, float *out_l, int out_bf16,
+                              void *stream);
+
 /* Zero the device status word (async). */
 int ts_clear_status(int *status, void *stream);
 /* Synchronise the stream, read and clear the status word. */

@@ -9,10 +9,11 @@ core):
 
 * Long-context decode with few kv heads shards the KEY axis: rank r holds keys
   [k_begin, k_begin + Sk_local) of every kv head, runs attn_flash_partial_stream on them
-  (masking by global key position), the per-row partials (m, l, acc) -- a few hundred KB --
-  are all-gathered over NVLink with NCCL, and every rank merges them with
-  attn_flash_combine_stream into the full output. This is the key loop of flash.c:798 split
-  across GPUs, with the online-softmax merge of flash.c:535-576 applied across shards.
+  (masking by global key position) straight into one packed block of per-row partials
+  (m, l, acc) -- a few hundred KB -- which one NCCL all-gather collects over NVLink, and every
+  rank merges them with attn_flash_combine_packed_stream into the full output. This is the key
+  loop of flash.c:798 split across GPUs, with the online-softmax merge of flash.c:535-576
+  applied across shards.
 
 The exchange uses only torch.distributed collectives, so the same code runs with the `gloo`
 backend on CPU tensors (the tests do that with a CPU stand-in for the partial kernel).
@@ -44,32 +45,40 @@ def key_shard(Sk: int, world: int, rank: int, align: int = ts.ATTN_GPU_KEY_TILE)
     return k0, k1 - k0
 
 
-def gather_partials(m: torch.Tensor, l: torch.Tensor, acc: torch.Tensor, group=None):
-    """All-gather the per-row partials of every rank: m, l [rows] and acc [rows, D] become
-    [world, rows] and [world, rows, D] (one NCCL all-gather each on GPU tensors)."""
+def packed_floats(rows: int, D: int) -> int:
+    """Floats of one rank's packed partial block: m [rows], l [rows], padding to a multiple of 4,
+    acc [rows][D] (attn_flash_packed_floats, restated so the CPU tests need no library)."""
+    return -(-2 * rows // 4) * 4 + rows * D
+
+
+def packed_views(buf: torch.Tensor, rows: int, D: int):
+    """(m, l, acc) views into one packed block (acc 16-byte aligned when buf is)."""
+    off = -(-2 * rows // 4) * 4
+    return buf[:rows], buf[rows:2 * rows], buf[off:off + rows * D].view(rows, D)
+
+
+def gather_packed(buf: torch.Tensor, group=None) -> torch.Tensor:
+    """One all-gather of every rank's packed block: [world * packed_floats] (the rank's own
+    block alone when there is no process group or a single rank)."""
     if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size(group) == 1:
-        return [t.contiguous().unsqueeze(0) for t in (m, l, acc)]  # one rank: nothing to exchange
+        return buf
     world = dist.get_world_size(group)
-    outs = []
-    for t in (m, l, acc):
-        t = t.contiguous()
-        o = torch.empty(world * t.numel(), dtype=t.dtype, device=t.device)
-        dist.all_gather_into_tensor(o, t.reshape(-1), group=group)
-        outs.append(o.view((world,) + tuple(t.shape)))
-    return outs
+    out = torch.empty(world * buf.numel(), dtype=buf.dtype, device=buf.device)
+    dist.all_gather_into_tensor(out, buf, group=group)
+    return out
 
 
 def sharded_decode(q, k_shard, v_shard, O, Hq: int, Hkv: int, Sq: int, Sk_total: int, k_begin: int, D: int,
                    causal: int, scratch, bk: int = ts.ATTN_BK_DEFAULT, group=None, stream=None):
     """Attention over a key axis split across the ranks of `group`. Every rank passes its own
     K/V shard ([Hkv][Sk_local][D], keys k_begin.. of the global axis) and the full Q; every rank
-    receives the full O [Hq*Sq*D] (fp32). Raises AttnError on a library error."""
+    receives the full O [Hq*Sq*D] (fp32). The partial kernel writes (m, l, acc) straight into one
+    packed block, one NCCL all-gather collects every rank's block and the combine merges them
+    from the gathered buffer. Raises AttnError on a library error."""
     rows = Hq * Sq
     Sk_local = k_shard.numel() // (Hkv * D)
-    dev = q.device
-    m = torch.empty(rows, dtype=torch.float32, device=dev)
-    l = torch.empty(rows, dtype=torch.float32, device=dev)
-    acc = torch.empty(rows, D, dtype=torch.float32, device=dev)
+    buf = torch.empty(packed_floats(rows, D), dtype=torch.float32, device=q.device)
+    m, l, acc = packed_views(buf, rows, D)
     if Sk_local > 0:
         rc = ts.attn_flash_partial_stream(q, k_shard, v_shard, m, l, acc, Hq, Hkv, Sq, Sk_local, Sk_total, k_begin,
                                           D, causal, bk, scratch, 0, stream)
@@ -79,9 +88,9 @@ def sharded_decode(q, k_shard, v_shard, O, Hq: int, Hkv: int, Sq: int, Sk_total:
         m.fill_(float("-inf"))
         l.zero_()
         acc.zero_()
-    all_m, all_l, all_acc = gather_partials(m, l, acc, group)
-    world = all_m.shape[0]
-    rc = ts.attn_flash_combine_stream(all_m, all_l, all_acc, world, rows, D, O, stream)
+    parts = gather_packed(buf, group)
+    nparts = parts.numel() // buf.numel()
+    rc = ts.attn_flash_combine_packed_stream(parts, nparts, rows, D, O, stream)
     if rc != ts.ATTN_OK:
-        raise ts.AttnError(rc, "attn_flash_combine_stream")
+        raise ts.AttnError(rc, "attn_flash_combine_packed_stream")
     return O
