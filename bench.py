@@ -20,6 +20,8 @@ Keys of the JSON line beyond the base contract:
                 streams take alternate steps, so one step's readback overlaps the next upload
   decode        a secondary HBM-bound line: BASELINE config 3 (GQA decode, B=64, Sk=8192), per GPU
   paged_decode  the same decode through attn_flash_paged_stream (64-key pages, shuffled table)
+  qkv_rope      the producer upstream of the path (attn_qkv_rope_stream: QKV split, q/k RMSNorm,
+                RoPE, cache write) at the config 5 prefill shape, HBM GB/s
   long_decode  BASELINE config 5 decode (B=4, Hq=64, Hkv=8, Sk=131072) with the key axis split
                 over all ranks: partial attention per rank into one packed (m, l, acc) block, one
                 NCCL all-gather of the blocks, merge on every rank (transfer_station_b200.multigpu)
@@ -479,6 +481,55 @@ def run_ours(args, w) -> None:
                       "ms_per_step": pms, "frac_of_measured_hbm": pach / peaks["hbm_gbs"], "steps": psteps}
         del pq, pk, pv, table, lens, po
 
+    # ---------------- the QKV producer (attn_qkv_rope_stream) at the config 5 prefill shape
+    producer_line = None
+    if not args.no_producer:
+        rB, rS, rHq, rHkv, rD = 4, 16384, 64, 8, 128
+        rT, rH = rB * rS, rHq + 2 * rHkv
+        g = torch.Generator(device=dev)
+        g.manual_seed(5)
+        rqkv = torch.randn(rT * rH * rD, device=dev, generator=g).to(torch.bfloat16).view(torch.int16)
+        rpos = torch.arange(rS, dtype=torch.int32, device=dev).repeat(rB)
+        rqw = (1.0 + 0.1 * torch.randn(rD, device=dev, generator=g)).to(torch.bfloat16).view(torch.int16)
+        rkw = (1.0 + 0.1 * torch.randn(rD, device=dev, generator=g)).to(torch.bfloat16).view(torch.int16)
+        rcs = torch.empty(rS * rD, dtype=torch.float32, device=dev)
+        if ts.attn_rope_table_stream(rcs, rS, rD, 1e6, stream) != ts.ATTN_OK:
+            raise ts.AttnError(ts.ATTN_ERR_ARGS, "attn_rope_table_stream")
+        rq = torch.empty(rT * rHq * rD, dtype=torch.int16, device=dev)
+        rk = torch.empty(rB * rHkv * rS * rD, dtype=torch.int16, device=dev)
+        rv = torch.empty_like(rk)
+
+        def producer_step():
+            rc = ts.attn_qkv_rope_stream(rqkv, rpos, rcs, rS, rqw, rkw, 1e-6, rB, rS, rHq, rHkv, rD, rD,
+                                         ts.ATTN_ROPE_NEOX, rq, rk, rv, rS, scratch, stream)
+            if rc != ts.ATTN_OK:
+                raise ts.AttnError(rc, "attn_qkv_rope_stream")
+
+        rsteps = max(3, min(args.steps, 100))
+        for _ in range(3):
+            producer_step()
+        barrier()
+        e0.record(stream)
+        for _ in range(rsteps):
+            producer_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        rms_ = max_over_ranks(e0.elapsed_time(e1)) / rsteps
+        rc, code = ts.attn_flash_status(scratch, stream)
+        if rc != ts.ATTN_OK:
+            raise ts.AttnError(rc, f"producer device status {code}")
+        # qkv read + Q/K/V written, plus each token's position and cos/sin table row
+        rby = 2.0 * rT * rH * rD * 2 + rT * 4 + rT * rD * 4
+        rach = rby / (rms_ / 1e3) / 1e9
+        producer_line = {"workload": "qwen3_qkv_rope_b4_s16384",
+                         "desc": "config 5 prefill shape (B4, Hq64/Hkv8, D128): fused QKV split + q/k RMSNorm + "
+                                 "NeoX RoPE (theta 1e6) + contiguous cache write, attn_qkv_rope_stream",
+                         "value": world * rach, "unit": "GB/s", "per_gpu_gbs": rach, "ms_per_step": rms_,
+                         "frac_of_measured_hbm": rach / peaks["hbm_gbs"], "bytes_per_step": rby, "steps": rsteps,
+                         "l2": "2.7 GB moved per step > L2"}
+        del rqkv, rpos, rqw, rkw, rcs, rq, rk, rv
+
     # ---------------- long-context decode, key axis split over the ranks (NCCL merge)
     long_line = None
     if not args.no_decode:
@@ -545,6 +596,7 @@ def run_ours(args, w) -> None:
             "decode": decode_line,
             "paged_decode": paged_line,
             "long_decode": long_line,
+            "qkv_rope": producer_line,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -557,6 +609,7 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-producer", action="store_true", help="skip the QKV producer line")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

@@ -16,12 +16,15 @@ import oracle
 import transfer_station_b200 as ts
 
 REPO = Path(__file__).resolve().parent.parent
-HEADER = REPO / "include" / "attn_flash.h"
+HEADERS = sorted((REPO / "include").glob("*.h"))
+
+
+def _header_text() -> str:
+    return re.sub(r"/\*.*?\*/", "", "\n".join(h.read_text() for h in HEADERS), flags=re.S)
 
 
 def declared_functions() -> set[str]:
-    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
-    return set(re.findall(r"\b(attn_flash\w*)\s*\(", text))
+    return set(re.findall(r"\b(attn_\w+)\s*\(", _header_text()))
 
 
 def test_library_exports_every_declared_symbol(built_lib):
@@ -34,9 +37,8 @@ def test_library_exports_every_declared_symbol(built_lib):
 
 def declared_arity() -> dict[str, int]:
     """Parameter count of every function prototype in the header."""
-    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
     out = {}
-    for name, params in re.findall(r"\b(attn_flash\w*)\s*\(([^)]*)\)\s*;", text):
+    for name, params in re.findall(r"\b(attn_\w+)\s*\(([^)]*)\)\s*;", _header_text()):
         params = params.strip()
         out[name] = 0 if params in ("", "void") else params.count(",") + 1
     return out
@@ -153,3 +155,48 @@ def test_missing_library_raises_no_fallback(tmp_path):
 
 def test_kernel_launch_counter_starts_at_zero(built_lib):
     assert isinstance(ts.attn_flash_kernel_launches(), int)
+
+
+def _rope_call(paged=False, **kw):
+    a = dict(qkv=1 << 20, pos=1 << 20, cs=1 << 20, max_pos=64, qw=None, kw=None, eps=1e-6, B=2, S=4, Hq=8, Hkv=2,
+             D=128, rot=128, style=ts.ATTN_ROPE_NEOX, Q=1 << 20, K=1 << 20, V=1 << 20, cache_len=64, bt=1 << 20,
+             ps=16, npages=4, maxp=4, scratch=1 << 20)
+    a.update(kw)
+    L = ts.load_library()
+    head = (a["qkv"], a["pos"], a["cs"], a["max_pos"], a["qw"], a["kw"], a["eps"], a["B"], a["S"], a["Hq"],
+            a["Hkv"], a["D"], a["rot"], a["style"], a["Q"], a["K"], a["V"])
+    if paged:
+        return L.attn_qkv_rope_paged_stream(*head, a["bt"], a["ps"], a["npages"], a["maxp"], a["scratch"], None)
+    return L.attn_qkv_rope_stream(*head, a["cache_len"], a["scratch"], None)
+
+
+@pytest.mark.parametrize("bad", [dict(D=96), dict(D=32), dict(rot=8), dict(rot=256), dict(rot=-16), dict(style=2),
+                                 dict(qkv=None), dict(Q=None), dict(pos=None), dict(scratch=None), dict(cs=None),
+                                 dict(max_pos=0), dict(cache_len=0), dict(Hq=0), dict(Hkv=0), dict(B=-1),
+                                 dict(qw=1 << 20, eps=-1.0), dict(kw=1 << 20, eps=float("nan"))])
+def test_rope_argument_validation(built_lib, bad):
+    assert _rope_call(**bad) == ts.ATTN_ERR_ARGS
+
+
+@pytest.mark.parametrize("bad", [dict(bt=None), dict(ps=0), dict(npages=0), dict(maxp=0), dict(D=80)])
+def test_rope_paged_argument_validation(built_lib, bad):
+    assert _rope_call(paged=True, **bad) == ts.ATTN_ERR_ARGS
+
+
+@pytest.mark.parametrize("bad", [dict(qkv=(1 << 20) + 8), dict(K=(1 << 20) + 2), dict(cs=(1 << 20) + 4),
+                                 dict(qw=(1 << 20) + 8), dict(scratch=(1 << 20) + 16)])
+def test_rope_alignment(built_lib, bad):
+    assert _rope_call(**bad) == ts.ATTN_ERR_ALIGN
+
+
+def test_rope_needs_no_table_without_rotation(built_lib):
+    """rot = 0 (norm / layout only) takes no table; the call then fails only for want of a B200."""
+    torch = pytest.importorskip("torch")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert _rope_call(rot=0, cs=None, max_pos=0) == ts.ATTN_ERR_NOT_SM100
+    L = ts.load_library()
+    assert L.attn_rope_table_stream(1 << 20, 0, 128, 1e4, None) == ts.ATTN_ERR_ARGS
+    assert L.attn_rope_table_stream(1 << 20, 8, 24, 1e4, None) == ts.ATTN_ERR_ARGS
+    assert L.attn_rope_table_stream(1 << 20, 8, 64, 1.0, None) == ts.ATTN_ERR_ARGS
+    assert L.attn_rope_table_stream(1 << 20, 8, 64, 1e4, None) == ts.ATTN_ERR_NOT_SM100

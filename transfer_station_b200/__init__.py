@@ -26,6 +26,9 @@ ATTN_PARTIAL_ROWS = 65536
 ATTN_OUT_F32 = 0
 ATTN_OUT_BF16 = 1
 
+ATTN_ROPE_GPTJ = 0
+ATTN_ROPE_NEOX = 1
+
 ATTN_OK = 0
 ATTN_ERR_ARGS = -1
 ATTN_ERR_ALIGN = -2
@@ -33,7 +36,7 @@ ATTN_ERR_CUDA = -3
 ATTN_ERR_DEVICE = -4
 ATTN_ERR_NOT_SM100 = -5
 
-# Every symbol include/attn_flash.h declares, with its ctypes signature.
+# Every symbol include/*.h declares, with its ctypes signature.
 _u16p = ctypes.c_void_p
 _f32p = ctypes.c_void_p
 EXPORTS = {
@@ -59,6 +62,15 @@ EXPORTS = {
     "attn_flash_combine_packed_stream": (ctypes.c_int, [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p,
                                                         ctypes.c_void_p]),
     "attn_flash_noalloc": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 8 + [ctypes.c_void_p]),
+    # include/attn_qkv_rope.h
+    "attn_rope_table_stream": (ctypes.c_int, [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_void_p]),
+    "attn_qkv_rope_stream": (ctypes.c_int, [_u16p, ctypes.c_void_p, _f32p, ctypes.c_int, _u16p, _u16p, ctypes.c_float]
+                             + [ctypes.c_int] * 7 + [_u16p, _u16p, _u16p, ctypes.c_int, ctypes.c_void_p,
+                                                     ctypes.c_void_p]),
+    "attn_qkv_rope_paged_stream": (ctypes.c_int, [_u16p, ctypes.c_void_p, _f32p, ctypes.c_int, _u16p, _u16p,
+                                                  ctypes.c_float] + [ctypes.c_int] * 7
+                                   + [_u16p, _u16p, _u16p, ctypes.c_void_p] + [ctypes.c_int] * 3
+                                   + [ctypes.c_void_p, ctypes.c_void_p]),
 }
 
 _lib = None
@@ -144,6 +156,35 @@ def attn_flash_paged_stream(Q, K_pages, V_pages, block_table, seq_lens, O, B, Hq
     return int(load_library().attn_flash_paged_stream(
         _ptr(Q), _ptr(K_pages), _ptr(V_pages), _ptr(block_table), _ptr(seq_lens), _ptr(O), B, Hq, Hkv, Sq, D,
         int(causal), page_size, num_pages, max_pages, _ptr(scratch), _stream_handle(stream)))
+
+
+def attn_rope_table_stream(cos_sin, max_pos, rot, theta, stream=None) -> int:
+    """Fill cos_sin fp32 [max_pos][rot] (cos in columns [0, rot/2), sin after) for frequencies
+    theta^(-2i/rot). Returns the status."""
+    return int(load_library().attn_rope_table_stream(_ptr(cos_sin), max_pos, rot, float(theta),
+                                                      _stream_handle(stream)))
+
+
+def attn_qkv_rope_stream(qkv, positions, cos_sin, max_pos, q_norm_w, k_norm_w, eps, B, S, Hq, Hkv, D, rot, style,
+                         Q, K_cache, V_cache, cache_len, scratch, stream=None) -> int:
+    """Split a fused QKV projection [B*S][(Hq+2Hkv)*D] (bf16 bits), RMSNorm (optional weights)
+    and rotate q/k heads, write Q [B*Hq][S][D] and K/V rows positions[t] of the contiguous cache
+    [B*Hkv][cache_len][D]. Returns the status."""
+    return int(load_library().attn_qkv_rope_stream(
+        _ptr(qkv), _ptr(positions), _ptr(cos_sin), max_pos, _ptr(q_norm_w), _ptr(k_norm_w), float(eps), B, S, Hq,
+        Hkv, D, rot, style, _ptr(Q), _ptr(K_cache), _ptr(V_cache), cache_len, _ptr(scratch),
+        _stream_handle(stream)))
+
+
+def attn_qkv_rope_paged_stream(qkv, positions, cos_sin, max_pos, q_norm_w, k_norm_w, eps, B, S, Hq, Hkv, D, rot,
+                               style, Q, K_pages, V_pages, block_table, page_size, num_pages, max_pages, scratch,
+                               stream=None) -> int:
+    """attn_qkv_rope_stream writing K/V into page pools [num_pages][Hkv][page_size][D] through
+    block_table int32 [B][max_pages] (attn_flash_paged_stream's cache). Returns the status."""
+    return int(load_library().attn_qkv_rope_paged_stream(
+        _ptr(qkv), _ptr(positions), _ptr(cos_sin), max_pos, _ptr(q_norm_w), _ptr(k_norm_w), float(eps), B, S, Hq,
+        Hkv, D, rot, style, _ptr(Q), _ptr(K_pages), _ptr(V_pages), _ptr(block_table), page_size, num_pages,
+        max_pages, _ptr(scratch), _stream_handle(stream)))
 
 
 def attn_flash_packed_floats(rows: int, D: int) -> int:

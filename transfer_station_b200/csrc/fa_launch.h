@@ -74,6 +74,26 @@ int ts_launch_combine_strided(const float *m, const float *l, const float *acc, 
                               size_t ps_ml, size_t ps_acc, float *O, float *out_m, float *out_l, int out_bf16,
                               void *stream);
 
+/* The QKV producer (qkv_rope.cu): one validated call of attn_qkv_rope_stream or
+ * attn_qkv_rope_paged_stream. n_vec = B*S*(Hq + 2*Hkv) head vectors of D elements. */
+typedef struct ts_rope_problem {
+    const uint16_t *qkv;
+    const int *positions;
+    const float *cos_sin;
+    const uint16_t *q_norm_w, *k_norm_w;
+    uint16_t *Q, *K, *V;
+    const int *block_table; /* NULL: contiguous cache [B*Hkv][cache_len][D] */
+    int *status;
+    long long n_vec;
+    float eps;
+    int B, S, Hq, Hkv, D, rot, style, max_pos;
+    int cache_len;                         /* contiguous cache rows per (sequence, kv head) */
+    int page_size, num_pages, max_pages;   /* paged cache */
+} ts_rope_problem;
+
+int ts_launch_qkv_rope(const ts_rope_problem *p, void *stream);
+int ts_launch_rope_table(float *cos_sin, int max_pos, int rot, double theta, void *stream);
+
 /* Zero the device status word (async). */
 int ts_clear_status(int *status, void *stream);
 /* Synchronise the stream, read and clear the status word. */

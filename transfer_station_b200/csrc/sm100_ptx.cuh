@@ -21,6 +21,7 @@ enum : int {
     kDevErrTimeoutP = 1 << 3,      // MMA waited too long for a P tile
     kDevErrTimeoutDrain = 1 << 4,  // teardown waited too long for in-flight copies / MMAs
     kDevErrBadPage = 1 << 5,       // a paged K/V block table held a page id outside the pool
+    kDevErrBadPos = 1 << 6,        // a token position outside the rotary table or the key cache
 };
 
 // ~2 s: every wait in these kernels is on a producer inside the same CTA, which completes
@@ -117,6 +118,14 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm,
         " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
         : "memory");
+}
+
+// Untiled bulk copy global -> this CTA's shared memory, completing `bytes` on `bar`. Both
+// addresses 16-byte aligned, bytes a multiple of 16. No multicast.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+                 : "memory");
 }
 
 // ---------------------------------------------------------------- TMEM / tcgen05
