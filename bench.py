@@ -484,7 +484,7 @@ def run_ours(args, w) -> None:
     # ---------------- the QKV producer (attn_qkv_rope_stream) at the config 5 prefill shape
     producer_line = None
     if not args.no_producer:
-        rB, rS, rHq, rHkv, rD = 4, 16384, 64, 8, 128
+        rB, rS, rHq, rHkv, rD = args.producer_batch, 16384, 64, 8, 128
         rT, rH = rB * rS, rHq + 2 * rHkv
         g = torch.Generator(device=dev)
         g.manual_seed(5)
@@ -522,12 +522,12 @@ def run_ours(args, w) -> None:
         # qkv read + Q/K/V written, plus each token's position and cos/sin table row
         rby = 2.0 * rT * rH * rD * 2 + rT * 4 + rT * rD * 4
         rach = rby / (rms_ / 1e3) / 1e9
-        producer_line = {"workload": "qwen3_qkv_rope_b4_s16384",
-                         "desc": "config 5 prefill shape (B4, Hq64/Hkv8, D128): fused QKV split + q/k RMSNorm + "
+        producer_line = {"workload": f"qwen3_qkv_rope_b{rB}_s16384",
+                         "desc": f"config 5 prefill shape (B{rB}, Hq64/Hkv8, D128): fused QKV split + q/k RMSNorm + "
                                  "NeoX RoPE (theta 1e6) + contiguous cache write, attn_qkv_rope_stream",
                          "value": world * rach, "unit": "GB/s", "per_gpu_gbs": rach, "ms_per_step": rms_,
                          "frac_of_measured_hbm": rach / peaks["hbm_gbs"], "bytes_per_step": rby, "steps": rsteps,
-                         "l2": "2.7 GB moved per step > L2"}
+                         "l2": f"{rby / 1e9:.2f} GB moved per step > L2"}
         del rqkv, rpos, rqw, rkw, rcs, rq, rk, rv
 
     # ---------------- long-context decode, key axis split over the ranks (NCCL merge)
@@ -610,6 +610,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-producer", action="store_true", help="skip the QKV producer line")
+    ap.add_argument("--producer-batch", type=int, default=4,
+                    help="sequences of 16384 tokens in the producer line (4 = the config 5 prefill shape)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--e2e-steps", type=int, default=200)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
