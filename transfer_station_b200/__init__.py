@@ -1,7 +1,8 @@
 """transfer_station_b200 -- B200 (sm_100a) bf16 flash-attention forward behind flash.c's C API.
 
 The product is the in-tree shared library ``lib/libattn_flash_b200.so`` (C host layer +
-tcgen05/TMA/TMEM CUDA kernels) whose entry points are declared in ``include/attn_flash.h``.
+tcgen05/TMA/TMEM CUDA kernels) whose entry points are declared in ``include/attn_flash.h``
+(the attention path) and ``include/attn_qkv_rope.h`` (the QKV producer before it).
 This module is the thin Python mirror of that C ABI (ctypes), used by the tests and the
 benchmark: same names, same argument meaning, same error behaviour. It never computes
 anything itself -- if the library is missing it raises, there is no fallback.
