@@ -3,11 +3,13 @@
 // attention's [B*Hq][S][D] layout and K/V into a contiguous or paged key cache -- one pass over
 // HBM. Byte work, so no tensor cores; the design goal is to keep HBM busy in both directions.
 //
-// Pipeline (one persistent CTA pair per SM). The input is one flat array of head vectors
+// Pipeline (three persistent CTAs per SM: 72 registers, a 64 KB ring each -- occupancy is
+// what hides the per-token load latency). The input is one flat array of head vectors
 // (D bf16 each), so it is cut into 16 KB chunks of whole vectors. One producer thread streams
 // the CTA's chunks into a ring of shared-memory stages with untiled bulk copies
 // (cp.async.bulk, completion counted on an mbarrier per stage): the reads stay in flight no
-// matter how long the consumers take. Eight consumer warps take each stage: a head vector is
+// matter how long the consumers take. Eight consumer warps take each stage (the norm weights
+// sit in shared memory as fp32, loaded once per CTA): a head vector is
 // handled by G = D/16 lanes, 16 elements (two 16-byte shared loads) each; results go straight
 // to global memory with 16-byte stores. Each warp releases the stage as soon as its bytes are
 // in registers. A CTA streams one contiguous run of chunks, so a lane meets each token once in
