@@ -240,26 +240,29 @@ __global__ void __launch_bounds__(256) fa_combine_few(const float *__restrict__ 
 
 }  // namespace ts
 
-extern "C" int ts_num_sms(void) {
-    static int cached[64] = {0};
+// Per-device attribute caches. Host threads may call the library concurrently (one scratch
+// block each), so the cache slots are atomics; two threads filling a slot store the same value.
+static int cached_device_attr(std::atomic<int> (&cache)[64], cudaDeviceAttr attr, int on_error) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-    if (dev < 64 && cached[dev]) return cached[dev];
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
-    if (dev < 64) cached[dev] = n;
-    return n;
+    if (cudaGetDevice(&dev) != cudaSuccess) return on_error;
+    if (dev >= 0 && dev < 64) {
+        const int v = cache[dev].load(std::memory_order_relaxed);
+        if (v) return v;
+    }
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, attr, dev) != cudaSuccess) return on_error;
+    if (dev >= 0 && dev < 64) cache[dev].store(v, std::memory_order_relaxed);
+    return v;
+}
+
+extern "C" int ts_num_sms(void) {
+    static std::atomic<int> cached[64];
+    return cached_device_attr(cached, cudaDevAttrMultiProcessorCount, 0);
 }
 
 extern "C" int ts_cc_major(void) {
-    static int cached[64] = {0};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
-    if (dev < 64 && cached[dev]) return cached[dev];
-    int v = 0;
-    if (cudaDeviceGetAttribute(&v, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return -1;
-    if (dev < 64) cached[dev] = v;
-    return v;
+    static std::atomic<int> cached[64];
+    return cached_device_attr(cached, cudaDevAttrComputeCapabilityMajor, -1);
 }
 
 extern "C" int ts_launch_combine_strided(const float *m, const float *l, const float *acc, int nparts, int rows,
