@@ -614,6 +614,15 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 const float mb = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
                 redo = __any_sync(0xffffffffu, mb > m && (mb - m) * sl2 > kRescaleLog2);
                 if (redo) tmem_wait_st();  // the speculative P stores land before the exact ones
+            } else if (__all_sync(0xffffffffu, nv <= 0)) {
+                // No row of this warp sees any key of the block (a causal tile below the
+                // diagonal of its item's last block): P = 0, m, l and O stay as they are.
+                uint32_t zero[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) zero[u] = 0u;
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) tmem_st16(tS + cc * 16, zero);
+                redo = false;
             } else {
                 tmem_ld128(tS, sr);
             }
