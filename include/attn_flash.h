@@ -61,9 +61,11 @@ extern "C" {
 #define ATTN_ERR_DEVICE -4      /* the kernel reported a bounded wait that ran out (see scratch status) */
 #define ATTN_ERR_NOT_SM100 -5   /* the current device is not compute capability 10.x */
 
-/* Per-phase timers of flash.c:704-706. On the GPU the four phases run fused in one kernel,
- * so attn_flash() writes zeros into *tm when tm != NULL (packv is always 0: V is never
- * transposed -- the tensor core reads it in place). Time the kernel with CUDA events. */
+/* Per-phase timers of flash.c:704-706. The reference adds each phase's seconds into *tm on
+ * every call (flash.c:822-849), so a caller zeroes it once and accumulates. On the GPU the four
+ * phases run fused in one kernel (and V is never transposed: packv has no counterpart), so
+ * attn_flash() adds nothing: *tm keeps whatever the caller had accumulated. Time the kernel
+ * with CUDA events. */
 struct attn_times {
     double packv, qxk, softmax, sxv;
 };

@@ -222,3 +222,35 @@ def test_dropped_block_negative_control(cuda_dev):
     bad = oracle.attn_ref(Q, K, Vbad.reshape(-1), Hq, Hkv, Sq, Sk, D, 0, rows)
     c = oracle.cmp_rows(bad, out, Hq, Sq, D, rows)
     assert not oracle.passes(c)
+
+
+def test_blocking_call_leaves_phase_totals(cuda_dev):
+    """The blocking attn_flash(.., tm) (flash.c:727-729): the reference adds each phase's seconds
+    into *tm (flash.c:822-849) and its harness accumulates over calls; with the phases fused in
+    one kernel nothing is added, so a caller's running totals come back unchanged. The output is
+    the attention itself (tm = NULL and tm given alike)."""
+    import ctypes
+
+    import torch
+
+    import transfer_station_b200 as ts
+    from tests.gpu_util import scratch_for, to_dev
+
+    class AttnTimes(ctypes.Structure):
+        _fields_ = [("packv", ctypes.c_double), ("qxk", ctypes.c_double), ("softmax", ctypes.c_double),
+                    ("sxv", ctypes.c_double)]
+
+    Hq, Hkv, Sq, Sk, D = 8, 2, 64, 300, 64
+    Q, K, V = oracle.lcg_inputs(Hq, Hkv, Sq, Sk, D)
+    q, k, v = to_dev(Q, cuda_dev), to_dev(K, cuda_dev), to_dev(V, cuda_dev)
+    scratch = scratch_for(D, 128, cuda_dev)
+    rows = np.arange(Sq, dtype=np.int32)
+    ref = oracle.attn_ref(Q, K, V, Hq, Hkv, Sq, Sk, D, 1, rows)
+    tm = AttnTimes(1.5, 2.5, 3.5, 4.5)
+    L = ts.load_library()
+    for tmp in (ctypes.cast(ctypes.pointer(tm), ctypes.c_void_p), None):
+        o = torch.full((Hq * Sq * D,), float("nan"), dtype=torch.float32, device=cuda_dev)
+        L.attn_flash(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), Hq, Hkv, Sq, Sk, D, 1, 128,
+                     scratch.data_ptr(), 0, tmp)
+        check(ref, o.cpu().numpy(), Hq, Sq, D, rows, "blocking attn_flash")
+    assert (tm.packv, tm.qxk, tm.softmax, tm.sxv) == (1.5, 2.5, 3.5, 4.5)

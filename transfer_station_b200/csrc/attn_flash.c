@@ -306,7 +306,10 @@ void attn_flash(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *
     int rc = attn_flash_stream(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, scratch, v_prepacked, NULL);
     int code = 0;
     if (rc == ATTN_OK) rc = attn_flash_status(scratch, NULL, &code);
-    if (tm) memset(tm, 0, sizeof *tm);
+    /* flash.c:822-849 adds each phase's seconds into *tm (its harness zeroes it once and
+     * divides by the call count). The four phases run fused in one kernel here, so there is
+     * nothing to add: *tm is left as the caller's running totals stand. */
+    (void)tm;
     if (rc != ATTN_OK) {
         fprintf(stderr, "attn_flash: %s (device code %d)\n", attn_flash_strerror(rc), code);
         abort();
