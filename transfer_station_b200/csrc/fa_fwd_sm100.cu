@@ -39,6 +39,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <type_traits>
 
 #include "attn_flash.h"
@@ -801,15 +802,16 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// Looked up once (thread-safe static initialisation); nullptr if the driver lacks the entry.
 static EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
+    static const EncodeTiledFn fn = []() -> EncodeTiledFn {
         void *ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
         if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(ptr);
-    }
+            return reinterpret_cast<EncodeTiledFn>(ptr);
+        return nullptr;
+    }();
     return fn;
 }
 
@@ -834,13 +836,14 @@ static int launch_tc_inst(cudaStream_t st, const CUtensorMap &tmQ, const CUtenso
                           const TcParams &prm, dim3 grid) {
     using C = TcConfig<DP, NQT>;
     auto kern = fa_tc_kernel<DP, NQT, VT, GENERAL, PAGED>;
-    static int attr_done[64] = {0};
+    static std::atomic<int> attr_done[64];  // the shared-memory opt-in, once per device
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return ATTN_ERR_CUDA;
-    if (dev < 64 && !attr_done[dev]) {
+    const bool cached = dev >= 0 && dev < 64;
+    if (!cached || !attr_done[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
             return ATTN_ERR_CUDA;
-        attr_done[dev] = 1;
+        if (cached) attr_done[dev].store(1, std::memory_order_release);
     }
     kern<<<grid, C::THREADS, C::SMEM, st>>>(tmQ, tmK, tmV, prm);
     if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;

@@ -23,6 +23,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "attn_qkv_rope.h"
 #include "fa_launch.h"
 #include "sm100_ptx.cuh"
@@ -301,6 +303,36 @@ __global__ void rope_table_kernel(float *cs, int max_pos, int rot, double theta)
 
 }  // namespace ts
 
+// Once per device and kernel instance: opt in to the ring's shared memory and read how many CTAs
+// fit on an SM (0: not set up yet). Concurrent first calls both do the same work.
+template <int D, bool NEOX, bool PAGED>
+static int rope_resident() {
+    static std::atomic<int> resident[64];
+    auto kern = ts::qkv_rope_kernel<D, NEOX, PAGED>;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+    const bool cached = dev >= 0 && dev < 64;
+    if (cached) {
+        const int r = resident[dev].load(std::memory_order_acquire);
+        if (r > 0) return r;
+    }
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, ts::kRopeSmem) != cudaSuccess)
+        return -1;
+    int r = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, kern, ts::kRopeThreads, ts::kRopeSmem) != cudaSuccess ||
+        r < 1)
+        r = 1;
+    if (cached) resident[dev].store(r, std::memory_order_release);
+    return r;
+}
+
+template <int D>
+static int pick_rope_resident(const ts_rope_problem *p) {
+    const bool neox = p->style == ATTN_ROPE_NEOX, paged = p->block_table != nullptr;
+    if (neox) return paged ? rope_resident<D, true, true>() : rope_resident<D, true, false>();
+    return paged ? rope_resident<D, false, true>() : rope_resident<D, false, false>();
+}
+
 template <int D>
 static void (*pick_rope_kernel(const ts_rope_problem *p))(ts_rope_problem) {
     const bool neox = p->style == ATTN_ROPE_NEOX, paged = p->block_table != nullptr;
@@ -312,19 +344,14 @@ extern "C" int ts_launch_qkv_rope(const ts_rope_problem *p, void *stream) {
     if (p->n_vec <= 0) return ATTN_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     void (*kern)(ts_rope_problem) = nullptr;
+    int resident = 0;  // CTAs per SM: one persistent wave of them
     switch (p->D) {
-    case 64: kern = pick_rope_kernel<64>(p); break;
-    case 128: kern = pick_rope_kernel<128>(p); break;
-    case 256: kern = pick_rope_kernel<256>(p); break;
+    case 64: kern = pick_rope_kernel<64>(p), resident = pick_rope_resident<64>(p); break;
+    case 128: kern = pick_rope_kernel<128>(p), resident = pick_rope_resident<128>(p); break;
+    case 256: kern = pick_rope_kernel<256>(p), resident = pick_rope_resident<256>(p); break;
     default: return ATTN_ERR_ARGS;
     }
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, ts::kRopeSmem) != cudaSuccess)
-        return ATTN_ERR_CUDA;
-    int resident = 0;  // CTAs per SM: one persistent wave of them
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident, kern, ts::kRopeThreads, ts::kRopeSmem) !=
-            cudaSuccess ||
-        resident < 1)
-        resident = 1;
+    if (resident < 0) return ATTN_ERR_CUDA;
     const long long chunks = (p->n_vec * p->D * 2 + ts::kRopeChunk - 1) / ts::kRopeChunk;
     const long long wave = (long long)ts_num_sms() * resident;
     kern<<<(unsigned)(chunks < wave ? chunks : wave), ts::kRopeThreads, ts::kRopeSmem, st>>>(*p);
