@@ -18,6 +18,12 @@
  *
  * Nothing here allocates device memory. Every call is asynchronous on its stream except
  * attn_flash(), which keeps the reference's blocking, void-returning contract.
+ *
+ * Threads: like flash.c (re-entrant given one scratch block per calling thread,
+ * flash.c:588-592), any number of host threads may call these entry points at once as long as
+ * each uses its own scratch block; give each thread its own stream for the calls to overlap.
+ * The library's only shared state is a per-device cache of device attributes and the launch
+ * counter, both safe to use concurrently.
  */
 #ifndef ATTN_FLASH_B200_H
 #define ATTN_FLASH_B200_H
