@@ -18,6 +18,7 @@ Keys of the JSON line beyond the base contract:
   e2e           the same metric through the C ABI with pinned host buffers: every step copies
                 Q, K, V host->device and O device->host inside the timed region; two CUDA
                 streams take alternate steps, so one step's readback overlaps the next upload
+  causal_prefill  the headline prefill with causal masking on the same buffers (useful FLOPs)
   decode        a secondary HBM-bound line: BASELINE config 3 (GQA decode, B=64, Sk=8192), per GPU
   paged_decode  the same decode through attn_flash_paged_stream (64-key pages, shuffled table)
   qkv_rope      the producer upstream of the path (attn_qkv_rope_stream: QKV split, q/k RMSNorm,
@@ -356,6 +357,37 @@ def run_ours(args, w) -> None:
     roof["peak_source"] = peaks["source"] + (" burst" if not decode else " copy")
     roof["kernel"] = "ts::fa_tc_kernel (tcgen05 + TMA + TMEM)"
 
+    # ---------------- the same prefill with causal masking (bottom-right), same buffers
+    causal_line = None
+    if not decode and not causal and not args.no_causal:
+        cfl = flops(Hq, Sq, Sk, D, 1)
+
+        def cstep(i: int):
+            c = i % ncopy
+            rc = ts.attn_flash_stream(qs[c], ks[c], vs[c], os_[c], Hq, Hkv, Sq, Sk, D, 1, 128, scratch, 0, stream)
+            if rc != ts.ATTN_OK:
+                raise ts.AttnError(rc, "attn_flash_stream (causal)")
+
+        csteps = max(3, min(args.steps, 200))
+        for i in range(3):
+            cstep(i)
+        barrier()
+        e0.record(stream)
+        for i in range(csteps):
+            cstep(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        cms = max_over_ranks(e0.elapsed_time(e1)) / csteps
+        rc, code = ts.attn_flash_status(scratch, stream)
+        if rc != ts.ATTN_OK:
+            raise ts.AttnError(rc, f"causal device status {code}")
+        cach = cfl / (cms / 1e3) / 1e12
+        causal_line = {"workload": args.workload + "_causal", "value": world * cach, "unit": "TFLOP/s",
+                       "per_gpu_tflops": cach, "ms_per_step": cms,
+                       "frac_of_measured_peak": cach / peaks["bf16_tflops"], "flops_per_step": cfl,
+                       "flops": "useful (query i sees keys <= Sk - Sq + i)", "steps": csteps}
+
     # ---------------- e2e through the C ABI with pinned host buffers
     # Two CUDA streams take alternate steps, each with its own device buffers, pinned output
     # buffer and scratch block: step i's readback (device -> host) runs while step i+1's inputs
@@ -593,6 +625,7 @@ def run_ours(args, w) -> None:
                                 "buffers): a step's readback overlaps the next step's upload"},
             "gpu_launches": int(launches),
             "clocks": csum,
+            "causal_prefill": causal_line,
             "decode": decode_line,
             "paged_decode": paged_line,
             "long_decode": long_line,
@@ -610,6 +643,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-producer", action="store_true", help="skip the QKV producer line")
+    ap.add_argument("--no-causal", action="store_true", help="skip the causal prefill line")
     ap.add_argument("--producer-batch", type=int, default=4,
                     help="sequences of 16384 tokens in the producer line (4 = the config 5 prefill shape)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
