@@ -250,3 +250,36 @@ def test_bad_page_is_reported(cuda_dev):
     assert ts.attn_flash_status(scratch) == (ts.ATTN_ERR_DEVICE, 1 << 5)
     Qb = _bits(q).reshape(B * Hq, S, D)
     assert np.all(Qb[Hq:, 1] == SENTINEL) and not np.any(Qb[:Hq] == SENTINEL)
+
+
+def test_empty_batch_is_a_no_op(cuda_dev):
+    """B*S = 0 tokens: the call succeeds, launches nothing that writes, and reports a clean status."""
+    D = 128
+    q = torch.full((64,), SENTINEL, dtype=torch.int16, device=cuda_dev)
+    k = torch.full((64,), SENTINEL, dtype=torch.int16, device=cuda_dev)
+    v = torch.full_like(k, SENTINEL)
+    qkv = torch.zeros(8, dtype=torch.int16, device=cuda_dev)
+    pos = torch.zeros(1, dtype=torch.int32, device=cuda_dev)
+    cs = to_dev(orq.rope_table(4, D, 1e4), cuda_dev)
+    scratch = scratch_for(D, 128, cuda_dev)
+    for B, S in ((0, 5), (3, 0)):
+        rc = ts.attn_qkv_rope_stream(qkv, pos, cs, 4, None, None, 1e-6, B, S, 4, 2, D, D, orq.NEOX, q, k, v, 4,
+                                     scratch)
+        assert rc == ts.ATTN_OK
+        assert ts.attn_flash_status(scratch) == (ts.ATTN_OK, 0)
+    assert np.all(_bits(q) == SENTINEL) and np.all(_bits(k) == SENTINEL) and np.all(_bits(v) == SENTINEL)
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(6, 6), (5, 3), (1, 1)])
+def test_head_layouts(cuda_dev, Hq, Hkv):
+    """MHA (Hq = Hkv), a head count that is not a multiple of Hkv (the producer does not need
+    one), and a single head: every head lands where the oracle puts it, bit for bit."""
+    B, S, D, rot = 2, 11, 64, 64
+    qkv, _, _ = _inputs(B, S, Hq, Hkv, D, 50 + Hq + Hkv, False)
+    pos = np.tile(np.arange(S, dtype=np.int32), B)
+    table = orq.rope_table(S, rot, 1e4)
+    Q, K, V, st = _run_contig(cuda_dev, qkv, pos, table, None, None, 1e-6, B, S, Hq, Hkv, D, rot, orq.NEOX, S)
+    assert st == (ts.ATTN_OK, 0)
+    rQ, rK, rV = orq.produce(qkv, pos, table, None, None, 1e-6, B, S, Hq, Hkv, D, rot, orq.NEOX)
+    assert np.array_equal(Q, rQ)
+    assert np.array_equal(K, rK.transpose(0, 2, 1, 3)) and np.array_equal(V, rV.transpose(0, 2, 1, 3))
