@@ -254,3 +254,18 @@ def test_blocking_call_leaves_phase_totals(cuda_dev):
                      scratch.data_ptr(), 0, tmp)
         check(ref, o.cpu().numpy(), Hq, Sq, D, rows, "blocking attn_flash")
     assert (tm.packv, tm.qxk, tm.softmax, tm.sxv) == (1.5, 2.5, 3.5, 4.5)
+
+
+def test_rows_beyond_partial_capacity(cuda_dev):
+    """A decode step with more query rows (Hq*Sq = 70016) than the scratch block holds key-piece
+    partials for (ATTN_PARTIAL_ROWS = 65536): the plan must run every unit over its whole key
+    range (no split), 8752 work items on a persistent grid, and still match the fp32 reference."""
+    Hq, Hkv, Sk, D = 70016, 8752, 300, 64
+    import transfer_station_b200 as ts
+
+    assert Hq > ts.ATTN_PARTIAL_ROWS
+    Q, K, V = oracle.seeded_inputs(Hq, Hkv, 1, Sk, D, seed=6)
+    rows = np.arange(1, dtype=np.int32)
+    ref = oracle.attn_ref(Q, K, V, Hq, Hkv, 1, Sk, D, 0, rows)
+    out = run_gpu(Q, K, V, Hq, Hkv, 1, Sk, D, 0, dev=cuda_dev)
+    check(ref, out, Hq, 1, D, rows, "rows beyond the partial capacity")
