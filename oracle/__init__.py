@@ -20,7 +20,8 @@ HERE = Path(__file__).resolve().parent
 LIB = HERE / "liboracle.so"
 REF_LIB = HERE / "_ref" / "libflashref.so"
 REF_LIB_BQ64 = HERE / "_ref" / "libflashref_bq64.so"
-REF_DIR = Path(os.environ.get("TS_REFERENCE_DIR", "/root/reference"))
+# The reference checkout: TS_REFERENCE_DIR, else a `reference` directory beside the repository.
+REF_DIR = Path(os.environ.get("TS_REFERENCE_DIR") or (HERE.parent.parent / "reference")).resolve()
 
 _lib = None
 _ref = {}

@@ -78,7 +78,7 @@ void orc_fill_lcg(uint16_t *Q, size_t nq, uint16_t *K, size_t nk, uint16_t *V, s
 
 /* splitmix64 (Steele, Lea, Flood 2014) -> uniform doubles in (0, 1). */
 static uint64_t splitmix64(uint64_t *s) {
-    uint64_t z = (*s += 0x9e3779b97f4a7c15ull);
+    uint64_t z = (*s += 0x9e3779b97f4a7c15ull); /* ORC_SM64_GAMMA */
     z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
     z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
     return z ^ (z >> 31);
@@ -86,20 +86,36 @@ static uint64_t splitmix64(uint64_t *s) {
 
 static double u01(uint64_t *s) { return ((double)(splitmix64(s) >> 11) + 0.5) * (1.0 / 9007199254740992.0); }
 
-/* N(mean, sigma) by Box-Muller, two values per pair of uniforms, RNE to bf16. */
+/* N(mean, sigma) by Box-Muller, two values per pair of uniforms, RNE to bf16. splitmix64's
+ * state advances by a constant per draw, so pair p (draws 2p, 2p+1) starts from
+ * state + 2p * gamma: the pairs are filled in parallel with the same values as one
+ * sequential pass, and the state ends where that pass would leave it. */
+#define ORC_SM64_GAMMA 0x9e3779b97f4a7c15ull
 void orc_fill_normal(uint16_t *out, size_t n, uint64_t *state, float mean, float sigma) {
     const double two_pi = 6.283185307179586476925286766559;
-    size_t i = 0;
-    while (i < n) {
-        const double u1 = u01(state), u2 = u01(state);
+    const uint64_t s0 = *state;
+    const long long npairs = (long long)((n + 1) / 2);
+#pragma omp parallel for schedule(static)
+    for (long long pi = 0; pi < npairs; pi++) {
+        uint64_t st = s0 + (uint64_t)(2 * pi) * ORC_SM64_GAMMA;
+        const double u1 = u01(&st), u2 = u01(&st);
         const double r = sqrt(-2.0 * log(u1));
-        out[i++] = orc_f32_to_bf16((float)(mean + sigma * r * cos(two_pi * u2)));
-        if (i < n) out[i++] = orc_f32_to_bf16((float)(mean + sigma * r * sin(two_pi * u2)));
+        const size_t i = 2 * (size_t)pi;
+        out[i] = orc_f32_to_bf16((float)(mean + sigma * r * cos(two_pi * u2)));
+        if (i + 1 < n) out[i + 1] = orc_f32_to_bf16((float)(mean + sigma * r * sin(two_pi * u2)));
     }
+    *state = s0 + (uint64_t)(2 * npairs) * ORC_SM64_GAMMA;
 }
 
+/* One draw per element; parallel by the same state arithmetic. */
 void orc_fill_uniform(uint16_t *out, size_t n, uint64_t *state, float lo, float hi) {
-    for (size_t i = 0; i < n; i++) out[i] = orc_f32_to_bf16((float)(lo + (hi - lo) * u01(state)));
+    const uint64_t s0 = *state;
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < (long long)n; i++) {
+        uint64_t st = s0 + (uint64_t)i * ORC_SM64_GAMMA;
+        out[i] = orc_f32_to_bf16((float)(lo + (hi - lo) * u01(&st)));
+    }
+    *state = s0 + (uint64_t)n * ORC_SM64_GAMMA;
 }
 
 /* flash.c:262-314. Row order and float arithmetic order follow the reference exactly, so

@@ -1,6 +1,7 @@
 """Generates tests/golden/*.npz from the REFERENCE's own flash.c.
 
-Run in a container that has the reference sources (default /root/reference):
+Run in a container that has the reference sources (TS_REFERENCE_DIR, or a `reference`
+directory beside the repository):
 
     python tests/golden/make_golden.py
 

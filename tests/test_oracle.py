@@ -190,3 +190,39 @@ def test_combine_of_key_splits_equals_full():
     w = np.where(keep, np.exp(s - s.max(1, keepdims=True)), 0)
     want = (w / w.sum(1, keepdims=True)) @ v
     assert np.allclose(O, want, atol=1e-5)
+
+
+def _splitmix_seq(state: int, ndraws: int):
+    """splitmix64 (Steele, Lea, Flood 2014) as one sequential stream of uniform doubles."""
+    M = (1 << 64) - 1
+    out = []
+    for _ in range(ndraws):
+        state = (state + 0x9E3779B97F4A7C15) & M
+        z = state
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+        z ^= z >> 31
+        out.append(((z >> 11) + 0.5) / 9007199254740992.0)
+    return state, out
+
+
+@pytest.mark.parametrize("n", [1, 2, 7, 64, 1001])
+def test_seeded_generators_match_a_sequential_stream(n):
+    """The parallel fill (each element's draw computed from the state arithmetic) equals one
+    sequential splitmix64 pass, for even and odd counts, and leaves the state where that pass
+    would: Box-Muller pairs for the normal fill, one draw per element for the uniform fill."""
+    import ctypes
+
+    st = ctypes.c_uint64(12345)
+    got_n = oracle.normal_bf16(n, st, 0.5, 2.0)
+    got_u = oracle.uniform_bf16(n, st, -2.0, 2.0)
+    s, u = _splitmix_seq(12345, 2 * ((n + 1) // 2))
+    want_n = []
+    for p in range(0, len(u), 2):
+        r = np.sqrt(-2.0 * np.log(u[p]))
+        want_n += [0.5 + 2.0 * r * np.cos(2 * np.pi * u[p + 1]), 0.5 + 2.0 * r * np.sin(2 * np.pi * u[p + 1])]
+    s, u2 = _splitmix_seq(s, n)
+    want_u = [-2.0 + 4.0 * x for x in u2]
+    assert np.array_equal(got_n, oracle.f32_to_bf16(np.array(want_n[:n], np.float32)))
+    assert np.array_equal(got_u, oracle.f32_to_bf16(np.array(want_u, np.float32)))
+    assert st.value == s
