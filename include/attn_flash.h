@@ -188,7 +188,9 @@ int attn_flash_combine_packed_stream(const float *parts, int nparts, int rows, i
  * allocator. Accepts at most 4096 query rows (Hq*Sq) -- decode-shaped calls -- and returns
  * ATTN_ERR_ARGS beyond that. All calls on a device share the block: calls whose GPU work
  * overlaps race. The first call on a device looks the block up (make it before any stream
- * capture). Blocks until the work on `stream` is done; returns ATTN_OK or a status code. */
+ * capture); the address is kept until exit, so do not call it on a device again after
+ * cudaDeviceReset. Blocks until the work on `stream` is done; returns ATTN_OK or a status
+ * code. */
 int attn_flash_noalloc(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O, int Hq,
                        int Hkv, int Sq, int Sk, int D, int causal, int bk, int v_prepacked,
                        void *stream);

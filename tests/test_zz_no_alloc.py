@@ -32,6 +32,8 @@ CASES = [
     (16 * 16, 16, 1, 4096, 128, 0, 3),      # MQA decode, batch 16
     (8, 2, 200, 300, 64, 1, 5),             # small causal prefill (no split)
     (6, 3, 1, 1000, 36, 0, 6),              # head_dim not a multiple of 8: the general path
+    (4096, 512, 1, 8192, 128, 0, 7),        # exactly the 4096-row limit: two pieces no longer fit, no split
+    (2048, 256, 1, 8192, 128, 0, 8),        # 2048 rows: at most three pieces fit the block
 ]
 
 
@@ -45,6 +47,9 @@ def _noalloc(Q, K, V, Hq, Hkv, Sq, Sk, D, causal, dev):
 
 @pytest.mark.parametrize("case", CASES, ids=[f"Hq{c[0]}_Sq{c[2]}_Sk{c[3]}_D{c[4]}_c{c[5]}" for c in CASES])
 def test_noalloc_matches_scratch_entry_point(cuda_dev, case):
+    """Each call is checked twice: against attn_flash_stream on the same inputs, and against the
+    fp32 reference (attn_ref, flash.c:262-314) on its own, so a planning fault the two entry
+    points shared would still be caught."""
     Hq, Hkv, Sq, Sk, D, causal, seed = case
     rows = np.arange(Sq, dtype=np.int32)
     for call in range(2):  # two calls in a row, different data each time
@@ -52,13 +57,19 @@ def test_noalloc_matches_scratch_entry_point(cuda_dev, case):
         want = run_gpu(Q, K, V, Hq, Hkv, Sq, Sk, D, causal, dev=cuda_dev)
         got = _noalloc(Q, K, V, Hq, Hkv, Sq, Sk, D, causal, cuda_dev)
         c = oracle.cmp_rows(want, got, Hq, Sq, D, rows)
-        assert oracle.passes(c), f"call {call}: {c}"
+        assert oracle.passes(c), f"call {call} vs attn_flash_stream: {c}"
+        ref = oracle.attn_ref(Q, K, V, Hq, Hkv, Sq, Sk, D, causal, rows)
+        c = oracle.cmp_rows(ref, got, Hq, Sq, D, rows)
+        assert oracle.passes(c), f"call {call} vs fp32 reference: {c}"
 
 
 def test_noalloc_rejects_oversized_calls(cuda_dev):
-    """More than 4096 query rows is beyond the fixed block's stated limit: a clear error."""
+    """More than 4096 query rows is beyond the fixed block's stated limit: a clear error. So is
+    a K/V whose rows (Hkv * Sk) do not fit a 32-bit index, which the other entry points also
+    reject; neither call launches anything (the tensors are too small to be read)."""
     Hq, Hkv, Sq, Sk, D = 32, 8, 256, 256, 64
     q = torch.zeros(Hq * Sq * D, dtype=torch.int16, device=cuda_dev)
     k = torch.zeros(Hkv * Sk * D, dtype=torch.int16, device=cuda_dev)
     o = torch.zeros(Hq * Sq * D, dtype=torch.float32, device=cuda_dev)
     assert ts.attn_flash_noalloc(q, k, k, o, Hq, Hkv, Sq, Sk, D, 0, 128) == ts.ATTN_ERR_ARGS
+    assert ts.attn_flash_noalloc(q, k, k, o, 8, 8, 1, 1 << 28, D, 0, 128) == ts.ATTN_ERR_ARGS

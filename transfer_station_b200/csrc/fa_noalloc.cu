@@ -20,7 +20,10 @@
 //     streams, or different host threads) race on the block: serialise them.
 //   * The first call on a device looks up the block's device address with
 //     cudaGetSymbolAddress (under a mutex), with that device current. Make that first
-//     call before any stream capture begins.
+//     call before any stream capture begins. The address is kept for the life of the
+//     process: after cudaDeviceReset on a device the library's module is loaded anew and the
+//     block may move, so a process that resets a device must not call this entry point on
+//     that device again.
 //   * The call returns when its work has finished (it synchronises `stream`), so that a
 //     device-side failure can be reported in its return value.
 #include <cuda_runtime.h>
@@ -81,6 +84,7 @@ extern "C" int attn_flash_noalloc(const uint16_t *Q, const uint16_t *K, const ui
     }
     if (!Q || !K || !V || !O || Hq < 1 || Hkv < 1 || Hq % Hkv != 0 || Sq < 1 || Sk < 1 || D < 1 || D > ATTN_D_MAX)
         return ATTN_ERR_ARGS;
+    if ((long long)Hkv * Sk > 0x7fffffffLL) return ATTN_ERR_ARGS;  // K/V rows are indexed with int
     const long long rows = (long long)Hq * Sq;
     if (rows > kNoallocMaxRows) {
         fprintf(stderr,
