@@ -106,3 +106,57 @@ def test_unit_and_key_shards_partition():
         assert sum(k for _, k in sh) == Sk
         assert all(b % 128 == 0 or b == Sk for b, _ in sh)
         assert all(sh[r][0] + sh[r][1] == sh[r + 1][0] for r in range(world - 1))
+
+
+def _prefill_worker(rank, world, port, case, out_dir):
+    """A rank of the (batch x kv-head group) sharded prefill, with a CPU stand-in for
+    attn_flash_stream (oracle.attn_ref on the numpy views the library would receive), so the
+    real multigpu.sharded_prefill code chooses the units, offsets and sizes."""
+    import transfer_station_b200 as ts
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        B, Hq, Hkv, Sq, Sk, D, causal = case
+        Q, K, V = oracle.lcg_inputs(B * Hq, B * Hkv, Sq, Sk, D)
+        q = torch.from_numpy(Q.view(np.int16))
+        k = torch.from_numpy(K.view(np.int16))
+        v = torch.from_numpy(V.view(np.int16))
+        O = torch.full((B * Hq * Sq * D,), float("nan"), dtype=torch.float32)
+
+        def stand_in(qv, kv_, vv, ov, hq, hkv, sq, sk, d, c, bk, scratch, vp, stream):
+            ref = oracle.attn_ref(qv.numpy().view(np.uint16), kv_.numpy().view(np.uint16),
+                                  vv.numpy().view(np.uint16), hq, hkv, sq, sk, d, c)
+            ov.copy_(torch.from_numpy(ref))
+            return ts.ATTN_OK
+
+        ts.attn_flash_stream = stand_in  # this process only
+        s = multigpu.sharded_prefill(q, k, v, O, B, Hq, Hkv, Sq, Sk, D, causal, scratch=None)
+        np.save(os.path.join(out_dir, f"o{rank}.npy"), O.numpy())
+        np.save(os.path.join(out_dir, f"s{rank}.npy"), np.array(s, np.int64))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("case", [(2, 8, 2, 40, 56, 32, 1), (3, 4, 4, 16, 16, 16, 0), (1, 6, 3, 24, 30, 8, 0)])
+def test_sharded_prefill_two_ranks(tmp_path, case):
+    """Each rank writes exactly its units' rows of O (the others stay untouched), the ranks'
+    units partition the problem, and together they give the full attention."""
+    world = 2
+    mp.spawn(_prefill_worker, args=(world, _free_port(), case, str(tmp_path)), nprocs=world, join=True)
+    B, Hq, Hkv, Sq, Sk, D, causal = case
+    Q, K, V = oracle.lcg_inputs(B * Hq, B * Hkv, Sq, Sk, D)
+    want = oracle.attn_ref(Q, K, V, B * Hq, B * Hkv, Sq, Sk, D, causal)
+    full = np.full_like(want, np.nan)
+    spans = []
+    for r in range(world):
+        o = np.load(tmp_path / f"o{r}.npy")
+        s = multigpu.PrefillSlice(*np.load(tmp_path / f"s{r}.npy").tolist())
+        spans.append((s.u0, s.u1))
+        mine = np.zeros(o.size, bool)
+        mine[s.q_off:s.q_off + s.hq * Sq * D] = True
+        assert np.all(np.isnan(o[~mine])), f"rank {r} wrote outside its units"
+        full[mine] = o[mine]
+    assert spans[0][0] == 0 and spans[-1][1] == B * Hkv and spans[0][1] == spans[1][0]
+    assert np.array_equal(full, want)

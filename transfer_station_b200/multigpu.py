@@ -5,7 +5,7 @@ core):
 
 * Prefill shards by (batch x kv-head group): the units are independent -- every query head of
   a group reads only its kv head's K/V -- so each rank runs attn_flash on whole kv groups and
-  writes its own slice of O. No collective.
+  writes its own slice of O (sharded_prefill). No collective.
 
 * Long-context decode with few kv heads shards the KEY axis: rank r holds keys
   [k_begin, k_begin + Sk_local) of every kv head, runs attn_flash_partial_stream on them
@@ -20,6 +20,8 @@ backend on CPU tensors (the tests do that with a CPU stand-in for the partial ke
 """
 from __future__ import annotations
 
+from typing import NamedTuple
+
 import torch
 import torch.distributed as dist
 
@@ -32,6 +34,66 @@ def unit_shard(n_units: int, world: int, rank: int) -> tuple[int, int]:
     base, extra = divmod(n_units, world)
     start = rank * base + min(rank, extra)
     return start, start + base + (1 if rank < extra else 0)
+
+
+class PrefillSlice(NamedTuple):
+    """One rank's share of a prefill sharded by (batch x kv-head group) units: units [u0, u1) of
+    the B*Hkv units, as an attn_flash problem of hq query heads and hkv kv heads whose Q / O
+    start `q_off` elements into [B*Hq][Sq][D] and whose K / V start `kv_off` elements into
+    [B*Hkv][Sk][D]. Unit u is kv head u of that layout, and its query heads u*group ..
+    u*group + group - 1 (b*Hq + kv*group == (b*Hkv + kv)*group), so a rank's share is one
+    contiguous range of each tensor: no gather, no copy."""
+
+    u0: int
+    u1: int
+    hq: int
+    hkv: int
+    q_off: int
+    kv_off: int
+
+
+def prefill_slice(B: int, Hq: int, Hkv: int, Sq: int, Sk: int, D: int, world: int, rank: int) -> PrefillSlice:
+    """The (batch x kv-head group) units of a B-sequence prefill that `rank` of `world` runs:
+    flash.c's head loop (flash.c:779-782, kv = h / group) partitioned by kv head, every query
+    head of a group staying with the kv head it reads."""
+    if Hq % Hkv:
+        raise ValueError("Hq must be a multiple of Hkv")
+    group = Hq // Hkv
+    u0, u1 = unit_shard(B * Hkv, world, rank)
+    return PrefillSlice(u0, u1, (u1 - u0) * group, u1 - u0, u0 * group * Sq * D, u0 * Sk * D)
+
+
+def _rank_world(group, rank, world):
+    if rank is not None and world is not None:
+        return rank, world
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(group), dist.get_world_size(group)
+    return 0, 1
+
+
+def sharded_prefill(q, k, v, O, B: int, Hq: int, Hkv: int, Sq: int, Sk: int, D: int, causal: int, scratch,
+                    bk: int = ts.ATTN_BK_DEFAULT, group=None, stream=None, rank: int | None = None,
+                    world: int | None = None) -> PrefillSlice:
+    """Prefill of B sequences ([B*Hq][Sq][D] queries, [B*Hkv][Sk][D] keys and values, O
+    [B*Hq][Sq][D] fp32) sharded over the ranks of `group` by (batch x kv-head group) units.
+    The tensors have the full problem's layout on every rank, but a rank reads only its units'
+    Q, K and V and writes only its units' rows of O, through one attn_flash_stream call on
+    those contiguous ranges; no collective is issued (each rank's O rows are final where they
+    are). `rank` / `world` override the process group's (one process may then run every
+    rank's share in turn). Returns the rank's PrefillSlice; raises AttnError on a library error."""
+    rank, world = _rank_world(group, rank, world)
+    s = prefill_slice(B, Hq, Hkv, Sq, Sk, D, world, rank)
+    if s.hkv == 0:  # more ranks than units: nothing to do here
+        return s
+    nq, nkv = s.hq * Sq * D, s.hkv * Sk * D
+    qv = q.view(-1)[s.q_off:s.q_off + nq]
+    kv_ = k.view(-1)[s.kv_off:s.kv_off + nkv]
+    vv = v.view(-1)[s.kv_off:s.kv_off + nkv]
+    ov = O.view(-1)[s.q_off:s.q_off + nq]
+    rc = ts.attn_flash_stream(qv, kv_, vv, ov, s.hq, s.hkv, Sq, Sk, D, causal, bk, scratch, 0, stream)
+    if rc != ts.ATTN_OK:
+        raise ts.AttnError(rc, "attn_flash_stream (sharded prefill)")
+    return s
 
 
 def key_shard(Sk: int, world: int, rank: int, align: int = ts.ATTN_GPU_KEY_TILE) -> tuple[int, int]:
