@@ -26,6 +26,11 @@ Keys of the JSON line beyond the base contract:
   long_decode  BASELINE config 5 decode (B=4, Hq=64, Hkv=8, Sk=131072) with the key axis split
                 over all ranks: partial attention per rank into one packed (m, l, acc) block, one
                 NCCL all-gather of the blocks, merge on every rank (transfer_station_b200.multigpu)
+  sharded_prefill  BASELINE config 5 prefill (B=4, Hq=64, Hkv=8, Sq=Sk=16384) as ONE problem whose
+                32 (batch x kv-head group) units are split over the ranks (multigpu.sharded_prefill,
+                no collective): strong scaling, `value` = the whole problem's FLOPs / max-rank time
+  configs       every other BASELINE config on each GPU (config 2 at S=1024 and S=2048, config 4
+                MQA prefill B=8 and decode B=128), device-timed, each with its roofline fraction
   gpu_launches  kernels the library launched inside the timed region (its own counter)
   clocks        SM clocks / throttle reasons sampled by NVML during the timed region
 
@@ -93,6 +98,24 @@ def algo_bytes(Hq, Hkv, Sq, Sk, D) -> float:
 
 def is_decode(w) -> bool:
     return w[2] == 1
+
+
+def pool_copies(w) -> tuple[int, int]:
+    """(copies, bytes per copy) of the rotating input/output pool: enough Q/K/V/O sets to cover
+    twice the L2, so that every timed step reads its inputs from HBM."""
+    Hq, Hkv, Sq, Sk, D = w[:5]
+    set_bytes = 2 * Hq * Sq * D + 2 * 2 * Hkv * Sk * D + 4 * Hq * Sq * D
+    return max(1, -(-2 * L2_BYTES // set_bytes)), set_bytes
+
+
+def config_dict(name: str, w, world: int) -> dict:
+    """The `config` of the JSON line; both arms print the same one for the same workload."""
+    Hq, Hkv, Sq, Sk, D, causal = w[:6]
+    ncopy, set_bytes = pool_copies(w)
+    return {"workload": name, "global_batch": world, "seq_len": Sq, "Hq": Hq, "Hkv": Hkv, "head_dim": D,
+            "causal": bool(causal),
+            "parallelism": f"dp{world} (one sequence per GPU, sharded by batch x kv-head group, no collective)",
+            "l2": f"rotating pool of {ncopy} Q/K/V/O sets ({ncopy * set_bytes / 2**20:.0f} MiB >= 2x L2)"}
 
 
 def host_inputs(w):
@@ -228,6 +251,49 @@ def cpu_reference_sample(w, seconds: float, threads: int | None = None) -> dict:
             "seconds": dt}
 
 
+def cpu_attn_ref_sample(w, seconds: float, threads: int | None = None) -> dict:
+    """Times the reference's fp32 reference attention (attn_ref, flash.c:262-314) compiled
+    natively from the reference sources (oracle/_ref; the bit-exact restatement when that build
+    is absent) on a bounded sample of workload w, one (head, row-slice) per task, all host
+    threads. Its work is counted in the same unit as the kernel's (4 * D FLOPs per query-key
+    pair), so the two CPU figures compare directly."""
+    import oracle
+
+    Hq, Hkv, Sq, Sk, D, causal, *_ = w
+    group = Hq // Hkv
+    threads = threads or os.cpu_count() or 1
+    use_ref = oracle.ref_available(128)
+    Q, K, V = host_inputs(w)
+    rows = max(1, min(Sq, 4))
+
+    def task(t: int, nrows: int) -> float:
+        h = t % Hq
+        kv = h // group
+        r0 = (t * 97) % max(1, Sq - nrows + 1)
+        q = np.ascontiguousarray(Q.reshape(Hq, Sq, D)[h, r0:r0 + nrows])
+        k = np.ascontiguousarray(K.reshape(Hkv, Sk, D)[kv])
+        v = np.ascontiguousarray(V.reshape(Hkv, Sk, D)[kv])
+        idx = np.arange(nrows, dtype=np.int32)
+        if use_ref:
+            oracle.ref_attn_ref(q, k, v, 1, 1, nrows, Sk, D, causal, idx)
+        else:
+            oracle.attn_ref(q, k, v, 1, 1, nrows, Sk, D, causal, idx)
+        return flops(1, nrows, Sk, D, causal)
+
+    t0 = time.perf_counter()
+    task(0, rows)
+    one = max(time.perf_counter() - t0, 1e-4)
+    rows = int(max(1, min(Sq, rows * seconds / one / 4)))
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        t0 = time.perf_counter()
+        fl = sum(ex.map(lambda t: task(t, rows), range(threads * 4)))
+        dt = time.perf_counter() - t0
+    return {"value": fl / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+            "kind": "reference" if use_ref else "port",
+            "sample": f"attn_ref (flash.c:262-314, fp32, compiled natively): {threads * 4} tasks of 1 head x "
+                      f"{rows} query rows x Sk={Sk} on {threads} threads, {dt:.1f} s"}
+
+
 def run_reference(args, w) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -251,7 +317,8 @@ def run_reference(args, w) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * secs / max(1, args.steps),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic " + w[9],
-        "config": {"workload": args.workload, "global_batch": 1, "seq_len": Sq, "parallelism": "cpu threads"},
+        "config": config_dict(args.workload, w, args.gpus),
+        "execution": f"{threads} host threads, rank 0 only; a bounded sample of the workload per step",
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": r["kind"],
                          "sample": r["sample"]},
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -295,8 +362,7 @@ def run_ours(args, w) -> None:
     fl = flops(Hq, Sq, Sk, D, causal)
     by = algo_bytes(Hq, Hkv, Sq, Sk, D)
     Q, K, V = host_inputs(w)  # same seeded data on every rank; each rank owns its copy
-    set_bytes = Q.nbytes + K.nbytes + V.nbytes + Hq * Sq * D * 4
-    ncopy = max(1, -(-2 * L2_BYTES // set_bytes))  # rotating pool >= 2x L2: every step is L2-cold
+    ncopy, set_bytes = pool_copies(w)  # rotating pool >= 2x L2: every step is L2-cold
     qs = [torch.from_numpy(Q.view(np.int16)).to(dev) for _ in range(ncopy)]
     ks = [torch.from_numpy(K.view(np.int16)).to(dev) for _ in range(ncopy)]
     vs = [torch.from_numpy(V.view(np.int16)).to(dev) for _ in range(ncopy)]
@@ -599,11 +665,111 @@ def run_ours(args, w) -> None:
                      "merge": "one NCCL all-gather of packed (m, l, acc) fp32 blocks, then combine"}
         del lq, lk, lv, lo
 
+    def time_steps(fn, steps: int, what: str) -> float:
+        """ms per step of `fn(i)` over `steps` calls after 3 warm-up calls (CUDA events on the
+        launching stream, barrier and synchronize on both sides, max over ranks)."""
+        for i in range(3):
+            fn(i)
+        barrier()
+        e0.record(stream)
+        for i in range(steps):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t = max_over_ranks(e0.elapsed_time(e1)) / steps
+        rc, code = ts.attn_flash_status(scratch, stream)
+        if rc != ts.ATTN_OK:
+            raise ts.AttnError(rc, f"{what} device status {code}")
+        return t
+
+    def device_inputs(wl, seed: int, n: int):
+        """Seeded bf16 tensor of n elements with workload wl's distribution, made on the GPU."""
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        a, b = wl[8]
+        if wl[6] == "normal":
+            x = torch.randn(n, device=dev, generator=g) * b + a
+        else:
+            x = torch.rand(n, device=dev, generator=g) * (b - a) + a
+        return x.to(torch.bfloat16).view(torch.int16)
+
+    # ---------------- the other BASELINE configs on each GPU (device-timed)
+    config_lines = []
+    if not args.no_configs:
+        for name in ("qwen3_gqa_prefill_s1024", "qwen3_gqa_prefill_s2048", "mqa_prefill_b8_s2048",
+                     "mqa_decode_b128_sk4096"):
+            if name == args.workload:
+                continue
+            cw = WORKLOADS[name]
+            cHq, cHkv, cSq, cSk, cD, cc = cw[:6]
+            cn, _ = pool_copies(cw)
+            bufs = [(device_inputs(cw, 10 * j + 1, cHq * cSq * cD), device_inputs(cw, 10 * j + 2, cHkv * cSk * cD),
+                     device_inputs(cw, 10 * j + 3, cHkv * cSk * cD),
+                     torch.empty(cHq * cSq * cD, dtype=torch.float32, device=dev)) for j in range(cn)]
+
+            def cfg_step(i: int, bufs=bufs, a=(cHq, cHkv, cSq, cSk, cD, cc)):
+                tq, tk, tv, to = bufs[i % len(bufs)]
+                rc = ts.attn_flash_stream(tq, tk, tv, to, *a, 128, scratch, 0, stream)
+                if rc != ts.ATTN_OK:
+                    raise ts.AttnError(rc, f"attn_flash_stream ({name})")
+
+            cms = time_steps(cfg_step, max(3, min(args.steps, 200)), name)
+            if is_decode(cw):
+                work, unit, peak = algo_bytes(cHq, cHkv, cSq, cSk, cD) / 1e9, "GB/s", peaks["hbm_gbs"]
+            else:
+                work, unit, peak = flops(cHq, cSq, cSk, cD, cc) / 1e12, "TFLOP/s", peaks["bf16_tflops"]
+            per = work / (cms / 1e3)
+            config_lines.append({"workload": name, "desc": cw[9], "value": world * per, "unit": unit,
+                                 "per_gpu": per, "ms_per_step": cms, "frac_of_measured_peak": per / peak,
+                                 "bound": "hbm" if is_decode(cw) else "tensor",
+                                 "steps": max(3, min(args.steps, 200)),
+                                 "l2": f"rotating pool of {cn} sets (>= 2x L2)", "data": "synthetic, seeded on device"})
+            del bufs
+
+    # ---------------- config 5 prefill as ONE problem sharded over the ranks (strong scaling)
+    sharded_line = None
+    if not args.no_sharded:
+        from transfer_station_b200 import multigpu
+
+        sB, sHq, sHkv, sS, sD = 4, 64, 8, 16384, 128
+        sl = multigpu.prefill_slice(sB, sHq, sHkv, sS, sS, sD, world, rank)
+        # full-layout tensors; this rank fills and touches only its units' ranges
+        sq = torch.empty(sB * sHq * sS * sD, dtype=torch.int16, device=dev)
+        sk = torch.empty(sB * sHkv * sS * sD, dtype=torch.int16, device=dev)
+        sv = torch.empty_like(sk)
+        so = torch.empty(sB * sHq * sS * sD, dtype=torch.float32, device=dev)
+        lw = WORKLOADS["long_prefill_b4_s16384"]
+        if sl.hkv > 0:
+            sq[sl.q_off:sl.q_off + sl.hq * sS * sD] = device_inputs(lw, 40 + rank, sl.hq * sS * sD)
+            sk[sl.kv_off:sl.kv_off + sl.hkv * sS * sD] = device_inputs(lw, 50 + rank, sl.hkv * sS * sD)
+            sv[sl.kv_off:sl.kv_off + sl.hkv * sS * sD] = device_inputs(lw, 60 + rank, sl.hkv * sS * sD)
+
+        def sharded_step(i: int):
+            multigpu.sharded_prefill(sq, sk, sv, so, sB, sHq, sHkv, sS, sS, sD, 0, scratch, stream=stream,
+                                     rank=rank, world=world)
+
+        ssteps = max(3, min(args.steps, 20))
+        sms_ = time_steps(sharded_step, ssteps, "sharded prefill")
+        sfl = flops(sB * sHq, sS, sS, sD, 0)
+        sval = sfl / (sms_ / 1e3) / 1e12
+        sharded_line = {"workload": "long_prefill_b4_s16384_sharded",
+                        "desc": "BASELINE config 5 prefill (B=4, Hq=64, Hkv=8, D=128, Sq=Sk=16384) as one problem: "
+                                f"its {sB * sHkv} (batch x kv-head group) units split over {world} rank(s) "
+                                "(multigpu.sharded_prefill), no collective",
+                        "value": sval, "unit": "TFLOP/s", "per_gpu_tflops": sval / world, "ms_per_step": sms_,
+                        "frac_of_measured_peak_per_gpu": sval / world / peaks["bf16_tflops"],
+                        "flops_per_step": sfl, "units_this_rank": [sl.u0, sl.u1], "steps": ssteps,
+                        "scaling": "strong (fixed problem; ms_per_step is the slowest rank's)",
+                        "l2": "3.4 GB of Q/K/V/O per rank > L2"}
+        del sq, sk, sv, so
+
     # ---------------- CPU baseline (rank 0, N=1 only)
     cpu = None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         r = cpu_reference_sample(w, args.cpu_seconds)
         cpu = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
+        cpu["fp32_reference"] = cpu_attn_ref_sample(w, max(2.0, args.cpu_seconds / 2))
 
     csum = clocks.summary(h0, h1)
     if rank == 0:
@@ -612,10 +778,7 @@ def run_ours(args, w) -> None:
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": f"synthetic, seeded ({w[6]}, seed {w[7]}), bf16 RNE; {w[9]}",
-            "config": {"workload": args.workload, "global_batch": world, "seq_len": Sq, "Hq": Hq,
-                       "Hkv": Hkv, "head_dim": D, "causal": bool(causal),
-                       "parallelism": f"dp{world} (one sequence per GPU, sharded by batch x kv-head group, no collective)",
-                       "l2": f"rotating pool of {ncopy} Q/K/V/O sets ({ncopy * set_bytes / 2**20:.0f} MiB >= 2x L2)"},
+            "config": config_dict(args.workload, w, world),
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": int(Q.nbytes + K.nbytes + V.nbytes),
@@ -630,6 +793,8 @@ def run_ours(args, w) -> None:
             "paged_decode": paged_line,
             "long_decode": long_line,
             "qkv_rope": producer_line,
+            "sharded_prefill": sharded_line,
+            "configs": config_lines,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -651,6 +816,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the other BASELINE configs' lines")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the sharded config 5 prefill line")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     w = WORKLOADS[args.workload]
