@@ -113,14 +113,16 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int *s
 }
 
 // GENERAL=false: every work item is a whole unit that writes normalised O (plain prefill/decode
-// without splits); GENERAL=true adds key pieces and caller-partial output.
+// without splits); GENERAL=true adds key pieces and caller-partial output. NOQ=true is the
+// diagnostic build of attn_diag_wait_timeout only: its producer never loads Q, so the MMA
+// issuer's bounded wait for Q runs out and the whole CTA takes the abort path.
 //
 // Persistent: the grid has at most one CTA per SM and each CTA walks the work items
 // blockIdx.x, blockIdx.x + gridDim.x, ... (for causal masking in alternating directions over
 // the longest-first list, so the long and short units even out per CTA). Every barrier keeps
 // counting phases across items, so the next item's Q load, first QK and first softmax block
 // overlap the previous item's last PV and epilogue.
-template <int DP, int NQT, bool VT, bool GENERAL, bool PAGED>
+template <int DP, int NQT, bool VT, bool GENERAL, bool PAGED, bool NOQ = false>
 __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                  const __grid_constant__ CUtensorMap tmV, const TcParams p) {
@@ -373,14 +375,16 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                     ok = false;
                     break;
                 }
-                mbar_expect_tx(q_full, NQT * C::QTILE);
+                if constexpr (!NOQ) {
+                    mbar_expect_tx(q_full, NQT * C::QTILE);
 #pragma unroll
-                for (int t = 0; t < NQT; ++t)
+                    for (int t = 0; t < NQT; ++t)
 #pragma unroll
-                    for (int b = 0; b < NBOX_D; ++b)
-                        tma_load_3d(sQ + t * C::QTILE + b * BOX_ROWS128, &tmQ, q_full, b * 64,
-                                    it.row0 + t * kBM, kv);
-                q_inflight = true;
+                        for (int b = 0; b < NBOX_D; ++b)
+                            tma_load_3d(sQ + t * C::QTILE + b * BOX_ROWS128, &tmQ, q_full, b * 64,
+                                        it.row0 + t * kBM, kv);
+                    q_inflight = true;
+                }
                 const int nload = 2 * it.nblk;
                 for (int i = 0; i < nload; ++i, ++gl) {
                     const int slot = gl % NS;
@@ -831,11 +835,11 @@ static bool make_map_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t 
     return r == CUDA_SUCCESS;
 }
 
-template <int DP, int NQT, bool VT, bool GENERAL, bool PAGED>
+template <int DP, int NQT, bool VT, bool GENERAL, bool PAGED, bool NOQ = false>
 static int launch_tc_inst(cudaStream_t st, const CUtensorMap &tmQ, const CUtensorMap &tmK, const CUtensorMap &tmV,
                           const TcParams &prm, dim3 grid) {
     using C = TcConfig<DP, NQT>;
-    auto kern = fa_tc_kernel<DP, NQT, VT, GENERAL, PAGED>;
+    auto kern = fa_tc_kernel<DP, NQT, VT, GENERAL, PAGED, NOQ>;
     static std::atomic<int> attr_done[64];  // the shared-memory opt-in, once per device
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return ATTN_ERR_CUDA;
@@ -851,7 +855,7 @@ static int launch_tc_inst(cudaStream_t st, const CUtensorMap &tmQ, const CUtenso
     return ATTN_OK;
 }
 
-template <int DP, int NQT, bool VT>
+template <int DP, int NQT, bool VT, bool NOQ = false>
 static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     const int group = P->Hq / P->Hkv;
     const uint64_t rows = (uint64_t)group * P->Sq;
@@ -911,6 +915,11 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     prm.group = group;
     prm.head_units = (P->Sq % (kBM * NQT) == 0) ? P->Sq / (kBM * NQT) : 0;
     const int sms = ts_num_sms() > 0 ? ts_num_sms() : 1;
+    if constexpr (NOQ) {  // the diagnostic build: plain work plan only
+        prm.n_items = units;
+        prm.snake = 0;
+        return launch_tc_inst<DP, NQT, VT, false, false, true>(st, tmQ, tmK, tmV, prm, dim3(min(units, sms)));
+    }
     if (prm.n_direct == units && !prm.write_partials && !P->paged) {
         prm.n_items = units;
         prm.snake = prm.causal;
@@ -947,6 +956,14 @@ extern "C" int ts_tc_ctas_per_split(const fa_problem *P) {
     const int nqt = ts::nqt_for(P);
     const long long tiles = (rows + ts::kBM * nqt - 1) / (ts::kBM * nqt);
     return (int)(tiles * P->Hkv);
+}
+
+// attn_diag_wait_timeout's launch: the NOQ build at head_dim 128, one 128-row tile per unit.
+extern "C" int ts_launch_tc_noq(const fa_problem *P, void *stream) {
+    using namespace ts;
+    if (P->D != 128 || (long long)(P->Hq / P->Hkv) * P->Sq > kBM || P->paged || P->v_prepacked) return ATTN_ERR_ARGS;
+    if (encode_fn() == nullptr) return ATTN_ERR_CUDA;
+    return launch_tc<128, 1, false, true>(P, static_cast<cudaStream_t>(stream), 1);
 }
 
 extern "C" int ts_launch_tc(const fa_problem *P, void *stream) {

@@ -22,6 +22,7 @@ enum : int {
     kDevErrTimeoutDrain = 1 << 4,  // teardown waited too long for in-flight copies / MMAs
     kDevErrBadPage = 1 << 5,       // a paged K/V block table held a page id outside the pool
     kDevErrBadPos = 1 << 6,        // a token position outside the rotary table or the key cache
+    kDevErrTimeoutPeer = 1 << 7,   // a peer GPU's partials never arrived (multi-GPU merge)
 };
 
 // ~2 s: every wait in these kernels is on a producer inside the same CTA, which completes
