@@ -180,6 +180,45 @@ size_t attn_flash_packed_floats(int rows, int D);
 int attn_flash_combine_packed_stream(const float *parts, int nparts, int rows, int D, float *O,
                                      void *stream);
 
+/* ---- The key-split decode merged over NVLink with peer stores: one kernel per rank, no
+ * collective library. No counterpart in the reference (one call on one core); it distributes
+ * the online-softmax merge of flash.c:535-576 over the GPUs of one node. ----
+ *
+ * Each rank owns one exchange block of attn_flash_peer_block_bytes(world, Hq*Sq, D) bytes of its
+ * device memory, zeroed once before the first call, and maps every peer's block into its address
+ * space (attn_peer_export on the owner, attn_peer_import on the others: CUDA IPC, peer access
+ * enabled). */
+#define ATTN_PEERS_MAX 8           /* ranks of one merge (the GPUs of one node) */
+#define ATTN_PEER_HANDLE_BYTES 128 /* bytes of an exported block handle */
+
+/* Bytes of one rank's exchange block. Layout, the same on every rank: uint32 flags
+ * [ATTN_PEERS_MAX][128] (the epoch each rank's merge CTA c reached), then two buffers (epoch
+ * parity) of `world` slots, slot s holding rank s's packed partial (attn_flash_packed_floats(rows,
+ * D) floats: m [rows], l [rows], padding, acc [rows][D]) rounded up to 256 bytes. */
+size_t attn_flash_peer_block_bytes(int world, int rows, int D);
+
+/* Writes an ATTN_PEER_HANDLE_BYTES handle of the device block at dev_ptr (any block inside a
+ * cudaMalloc allocation) that other processes on the node can import. */
+int attn_peer_export(void *dev_ptr, void *handle);
+/* Maps a peer's exported block into this process (on the current device); *dev_ptr receives its
+ * address here. attn_peer_close(dev_ptr, handle) unmaps it. */
+int attn_peer_import(const void *handle, void **dev_ptr);
+int attn_peer_close(void *dev_ptr, const void *handle);
+
+/* attn_flash_partial_stream on this rank's key shard, then ONE merge kernel: it merges the
+ * shard's key pieces per row, stores the rank's (m, l, acc) into slot `rank` of every rank's
+ * exchange block over NVLink, raises its flags there, waits (bounded) until every rank's partials
+ * reached its own block, and writes the full attention O [Hq][Sq][D] fp32 -- on every rank.
+ * blocks[r] is rank r's exchange block as mapped in this process (blocks[rank] its own). epoch
+ * numbers the calls made with these blocks: 1 for the first call, +1 per call, the same on every
+ * rank, and every rank makes every call (a rank with an empty shard passes Sk_local = 0).
+ * A peer that never arrives ends the wait after ~2 s with ATTN_DEV_TIMEOUT_PEER in the status
+ * word (attn_flash_status). Requires Hq*Sq <= ATTN_PARTIAL_ROWS. */
+int attn_flash_decode_peers_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O,
+                                   int Hq, int Hkv, int Sq, int Sk_local, int Sk_total, int k_begin,
+                                   int D, int causal, int bk, void *scratch, void *const *blocks,
+                                   int world, int rank, unsigned int epoch, void *stream);
+
 /* attn_flash without a scratch argument, for callers that cannot allocate device memory (a
  * host whose device memory belongs to its own pool allocator, or a foreign-function binding
  * with nowhere to keep a device buffer between calls). No counterpart in the reference: its

@@ -119,3 +119,60 @@ def test_two_gpu_sharded_prefill(tmp_path):
     ref = oracle.attn_ref(Q, K, V, B * Hq, B * Hkv, S, S, D, 0, rows)
     c = oracle.cmp_rows(ref, full, B * Hq, S, D, rows)
     assert oracle.passes(c), c
+
+
+def _peer_worker(rank, world, port, out_path):
+    from datetime import timedelta
+
+    import transfer_station_b200 as ts
+    from transfer_station_b200 import multigpu
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    merge = None
+    try:
+        Hq, Hkv, Sq, Sk, D = 64, 8, 1, 65536, 128
+        merge = multigpu.PeerMerge(Hq * Sq, D, device=dev)
+        scratch = torch.empty(ts.attn_flash_scratch_bytes(D, 128), dtype=torch.uint8, device=dev)
+        outs = []
+        for step in range(3):  # epochs 1..3: both buffers, new data every step
+            Q, K, V = oracle.seeded_inputs(Hq, Hkv, Sq, Sk, D, seed=40 + step, a=0.0, b=0.5)
+            k0, kl = multigpu.key_shard(Sk, world, rank)
+            Ks = np.ascontiguousarray(K.reshape(Hkv, Sk, D)[:, k0:k0 + kl]).reshape(-1)
+            Vs = np.ascontiguousarray(V.reshape(Hkv, Sk, D)[:, k0:k0 + kl]).reshape(-1)
+            q = torch.from_numpy(Q.view(np.int16)).to(dev)
+            ks = torch.from_numpy(Ks.view(np.int16)).to(dev)
+            vs = torch.from_numpy(Vs.view(np.int16)).to(dev)
+            o = torch.full((Hq * Sq * D,), float("nan"), dtype=torch.float32, device=dev)
+            multigpu.sharded_decode_peers(q, ks, vs, o, Hq, Hkv, Sq, Sk, k0, D, 0, scratch, merge)
+            torch.cuda.synchronize()
+            rc, code = ts.attn_flash_status(scratch)
+            assert rc == ts.ATTN_OK, code
+            outs.append(o.cpu().numpy())
+        np.save(out_path + f".{rank}.npy", np.stack(outs))
+    finally:
+        if merge is not None:
+            merge.close()
+        dist.destroy_process_group()
+
+
+def test_two_gpu_decode_merged_by_peer_stores(tmp_path):
+    """The merge kernel's real exchange over NVLink: 2 ranks, 3 steps; every rank ends with the
+    full output, equal on both ranks and within tolerance of the fp32 reference."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    out = str(tmp_path / "o")
+    mp.spawn(_peer_worker, args=(2, _free_port(), out), nprocs=2, join=True)
+    Hq, Hkv, Sq, Sk, D = 64, 8, 1, 65536, 128
+    o0, o1 = np.load(out + ".0.npy"), np.load(out + ".1.npy")
+    assert np.array_equal(o0, o1)
+    rows = np.arange(Sq, dtype=np.int32)
+    for step in range(3):
+        Q, K, V = oracle.seeded_inputs(Hq, Hkv, Sq, Sk, D, seed=40 + step, a=0.0, b=0.5)
+        ref = oracle.attn_ref(Q, K, V, Hq, Hkv, Sq, Sk, D, 0, rows)
+        c = oracle.cmp_rows(ref, o0[step], Hq, Sq, D, rows)
+        assert oracle.passes(c), (step, c)

@@ -24,11 +24,25 @@ ATTN_GPU_KEY_TILE = 128
 ATTN_D_MAX = 256
 ATTN_PARTIAL_ROWS = 65536
 
+ATTN_PEERS_MAX = 8
+ATTN_PEER_HANDLE_BYTES = 128
+
 ATTN_OUT_F32 = 0
 ATTN_OUT_BF16 = 1
 
 ATTN_ROPE_GPTJ = 0
 ATTN_ROPE_NEOX = 1
+
+ATTN_DEV_TIMEOUT_Q = 1
+ATTN_DEV_TIMEOUT_KV = 2
+ATTN_DEV_TIMEOUT_S = 4
+ATTN_DEV_TIMEOUT_P = 8
+ATTN_DEV_TIMEOUT_DRAIN = 16
+ATTN_DEV_BAD_PAGE = 32
+ATTN_DEV_BAD_POS = 64
+ATTN_DEV_TIMEOUT_PEER = 128
+ATTN_DIAG_EXP2_POLY = 0
+ATTN_DIAG_EXP2_MUFU = 1
 
 ATTN_OK = 0
 ATTN_ERR_ARGS = -1
@@ -63,6 +77,18 @@ EXPORTS = {
     "attn_flash_combine_packed_stream": (ctypes.c_int, [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int, _f32p,
                                                         ctypes.c_void_p]),
     "attn_flash_noalloc": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 8 + [ctypes.c_void_p]),
+    "attn_flash_peer_block_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int, ctypes.c_int]),
+    "attn_peer_export": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "attn_peer_import": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "attn_peer_close": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "attn_flash_decode_peers_stream": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 9 +
+                                       [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_uint,
+                                        ctypes.c_void_p]),
+    # include/attn_flash_diag.h
+    "attn_diag_fill_tmem": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p]),
+    "attn_diag_exp2": (ctypes.c_int, [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "attn_diag_wait_timeout": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 4 +
+                               [ctypes.c_void_p, ctypes.c_void_p]),
     # include/attn_qkv_rope.h
     "attn_rope_table_stream": (ctypes.c_int, [_f32p, ctypes.c_int, ctypes.c_int, ctypes.c_double, ctypes.c_void_p]),
     "attn_qkv_rope_stream": (ctypes.c_int, [_u16p, ctypes.c_void_p, _f32p, ctypes.c_int, _u16p, _u16p, ctypes.c_float]
@@ -234,6 +260,58 @@ def attn_flash_noalloc(Q, K, V, O, Hq, Hkv, Sq, Sk, D, causal, bk, v_prepacked=0
     fixed 4 MiB device block is used), at most 4096 query rows, blocking. Returns the status."""
     return int(load_library().attn_flash_noalloc(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), Hq, Hkv, Sq, Sk, D, int(causal),
                                                  bk, int(v_prepacked), _stream_handle(stream)))
+
+
+def attn_flash_peer_block_bytes(world: int, rows: int, D: int) -> int:
+    return int(load_library().attn_flash_peer_block_bytes(world, rows, D))
+
+
+def attn_peer_export(block) -> bytes:
+    """The ATTN_PEER_HANDLE_BYTES handle of a device block (for peers to import)."""
+    buf = ctypes.create_string_buffer(ATTN_PEER_HANDLE_BYTES)
+    rc = load_library().attn_peer_export(_ptr(block), buf)
+    if rc != ATTN_OK:
+        raise AttnError(rc, "attn_peer_export")
+    return buf.raw
+
+
+def attn_peer_import(handle: bytes) -> int:
+    """Maps a peer's exported block into this process; returns its device address here."""
+    out = ctypes.c_void_p(0)
+    rc = load_library().attn_peer_import(ctypes.create_string_buffer(handle, ATTN_PEER_HANDLE_BYTES),
+                                         ctypes.byref(out))
+    if rc != ATTN_OK:
+        raise AttnError(rc, "attn_peer_import")
+    return int(out.value)
+
+
+def attn_peer_close(addr: int, handle: bytes) -> int:
+    return int(load_library().attn_peer_close(addr, ctypes.create_string_buffer(handle, ATTN_PEER_HANDLE_BYTES)))
+
+
+def attn_flash_decode_peers_stream(Q, K, V, O, Hq, Hkv, Sq, Sk_local, Sk_total, k_begin, D, causal, bk, scratch,
+                                   blocks, world, rank, epoch, stream=None) -> int:
+    """`blocks`: every rank's exchange block as device addresses in this process (ints)."""
+    arr = (ctypes.c_void_p * len(blocks))(*blocks)
+    return int(load_library().attn_flash_decode_peers_stream(
+        _ptr(Q), _ptr(K), _ptr(V), _ptr(O), Hq, Hkv, Sq, Sk_local, Sk_total, k_begin, D, int(causal), bk,
+        _ptr(scratch), arr, world, rank, epoch, _stream_handle(stream)))
+
+
+def attn_diag_fill_tmem(bits: int, stream=None) -> int:
+    """Diagnostic: write the 32-bit pattern `bits` into all tensor memory of every SM."""
+    return int(load_library().attn_diag_fill_tmem(bits & 0xFFFFFFFF, _stream_handle(stream)))
+
+
+def attn_diag_exp2(x, y, n, method, stream=None) -> int:
+    """Diagnostic: y = 2^x by the attention kernel's polynomial (method 0) or MUFU (method 1)."""
+    return int(load_library().attn_diag_exp2(_ptr(x), _ptr(y), n, method, _stream_handle(stream)))
+
+
+def attn_diag_wait_timeout(Q, K, V, O, Hq, Hkv, Sq, Sk, scratch, stream=None) -> int:
+    """Diagnostic: the attention kernel with its Q load left out, so a bounded wait runs out."""
+    return int(load_library().attn_diag_wait_timeout(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), Hq, Hkv, Sq, Sk,
+                                                     _ptr(scratch), _stream_handle(stream)))
 
 
 def attn_flash_combine_stream(m, l, acc, nparts, rows, D, O, stream=None) -> int:

@@ -28,7 +28,7 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-r
 CC = os.environ.get("CC", "gcc")
 CC_FLAGS = ["-O2", "-std=c11", "-fPIC", "-Wall", "-Wextra"]
 
-CU_SOURCES = ["fa_fwd_sm100.cu", "fa_aux.cu", "fa_noalloc.cu", "qkv_rope.cu"]
+CU_SOURCES = ["fa_fwd_sm100.cu", "fa_aux.cu", "fa_noalloc.cu", "fa_diag.cu", "fa_peer.cu", "qkv_rope.cu"]
 C_SOURCES = ["attn_flash.c", "attn_qkv_rope.c"]
 
 

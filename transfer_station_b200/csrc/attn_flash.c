@@ -269,6 +269,52 @@ int attn_flash_partial_stream(const uint16_t *Q, const uint16_t *K, const uint16
     return ts_run(&p, scratch, stream);
 }
 
+int attn_flash_decode_peers_stream(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O, int Hq,
+                                   int Hkv, int Sq, int Sk_local, int Sk_total, int k_begin, int D, int causal, int bk,
+                                   void *scratch, void *const *blocks, int world, int rank, unsigned int epoch,
+                                   void *stream) {
+    attn_bk_check(bk, "attn_flash_decode_peers");
+    if (!O || !blocks || world < 1 || world > ATTN_PEERS_MAX || rank < 0 || rank >= world || epoch == 0 ||
+        Sk_local < 0 || k_begin < 0 || Sk_total < 1 || (long long)k_begin + Sk_local > Sk_total)
+        return ATTN_ERR_ARGS;
+    for (int r = 0; r < world; ++r)
+        if (!blocks[r]) return ATTN_ERR_ARGS;
+        else if (((uintptr_t)blocks[r]) & 255u) return ATTN_ERR_ALIGN;
+    /* validated as the whole key axis when this shard is empty (K and V are not read then) */
+    int rc = ts_validate(Q, Sk_local > 0 ? K : Q, Sk_local > 0 ? V : Q, Hq, Hkv, Sq, Sk_local > 0 ? Sk_local : 1, D,
+                         scratch);
+    if (rc != ATTN_OK) return rc;
+    if ((long long)Hq * Sq > ATTN_PARTIAL_ROWS) return ATTN_ERR_ARGS;
+    ts_scratch s;
+    ts_scratch_layout(scratch, D, &s);
+    rc = ts_clear_status(s.status, stream);
+    if (rc != ATTN_OK) return rc;
+    int nparts = 0;
+    if (Sk_local > 0) {
+        fa_problem p;
+        ts_fill(&p, Q, K, V, Hq, Hkv, Sq, Sk_local, D, causal, 0);
+        p.Sk_total = Sk_total;
+        p.k_begin = k_begin;
+        p.status = s.status;
+        ts_plan(&p);
+        if (p.n_direct > 0) { /* a prefill tail split: run every unit whole instead */
+            p.nsplit = 1;
+            p.n_direct = 0;
+            p.row_base = 0;
+            p.keys_per_split = ((Sk_local + ATTN_GPU_KEY_TILE - 1) / ATTN_GPU_KEY_TILE) * ATTN_GPU_KEY_TILE;
+        }
+        /* every piece lands in the scratch partial arrays as [piece][row] */
+        p.write_partials = 1;
+        p.part_m = p.out_m = s.m;
+        p.part_l = p.out_l = s.l;
+        p.part_acc = p.out_acc = s.acc;
+        rc = ts_launch_attention_pieces(&p, stream);
+        if (rc != ATTN_OK) return rc;
+        nparts = p.nsplit;
+    }
+    return ts_launch_peer_merge(s.m, s.l, s.acc, nparts, Hq * Sq, D, O, blocks, world, rank, epoch, s.status, stream);
+}
+
 int attn_flash_combine_stream(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
                               float *O, void *stream) {
     if (!m || !l || !acc || !O || nparts < 1 || rows < 0 || D < 1 || D > ATTN_D_MAX) return ATTN_ERR_ARGS;

@@ -336,6 +336,10 @@ static int launch_simt(const fa_problem *P, void *stream, int partial) {
     return ATTN_OK;
 }
 
+extern "C" int ts_launch_attention_pieces(const fa_problem *P, void *stream) {
+    return ts_tc_supported(P) ? ts_launch_tc(P, stream) : launch_simt(P, stream, 1);
+}
+
 extern "C" int ts_launch_attention(const fa_problem *P, void *stream) {
     const bool tc = ts_tc_supported(P) != 0;
     int rc = tc ? ts_launch_tc(P, stream) : launch_simt(P, stream, (P->nsplit > 1 || P->write_partials) ? 1 : 0);

@@ -74,6 +74,16 @@ int ts_launch_combine_strided(const float *m, const float *l, const float *acc, 
                               size_t ps_ml, size_t ps_acc, float *O, float *out_m, float *out_l, int out_bf16,
                               void *stream);
 
+/* The main attention kernel alone (tensor-core or general path), without the merge of split
+ * key pieces that ts_launch_attention adds: the pieces stay in the partial arrays. */
+int ts_launch_attention_pieces(const fa_problem *p, void *stream);
+
+/* The key-split decode's merge over NVLink (fa_peer.cu): nparts local key pieces [nparts][rows]
+ * (0: an empty shard) -> every rank's exchange block -> O [rows][D] fp32. */
+int ts_launch_peer_merge(const float *m, const float *l, const float *acc, int nparts, int rows, int D,
+                         float *O, void *const *blocks, int world, int rank, unsigned epoch, int *status,
+                         void *stream);
+
 /* The QKV producer (qkv_rope.cu): one validated call of attn_qkv_rope_stream or
  * attn_qkv_rope_paged_stream. n_vec = B*S*(Hq + 2*Hkv) head vectors of D elements. */
 typedef struct ts_rope_problem {

@@ -15,7 +15,12 @@ core):
   loop of flash.c:798 split across GPUs, with the online-softmax merge of flash.c:535-576
   applied across shards.
 
-The exchange uses only torch.distributed collectives, so the same code runs with the `gloo`
+  Two ways to merge: `sharded_decode` (the partial kernel into a packed block, one NCCL
+  all-gather, the combine kernel) and `sharded_decode_peers` with a `PeerMerge` (the partial
+  kernel, then ONE merge kernel that stores each rank's partials straight into every peer's
+  exchange block over NVLink, signals with flags, and merges: no collective per step).
+
+The NCCL path uses only torch.distributed collectives, so the same code runs with the `gloo`
 backend on CPU tensors (the tests do that with a CPU stand-in for the partial kernel).
 """
 from __future__ import annotations
@@ -155,4 +160,59 @@ def sharded_decode(q, k_shard, v_shard, O, Hq: int, Hkv: int, Sq: int, Sk_total:
     rc = ts.attn_flash_combine_packed_stream(parts, nparts, rows, D, O, stream)
     if rc != ts.ATTN_OK:
         raise ts.AttnError(rc, "attn_flash_combine_packed_stream")
+    return O
+
+
+class PeerMerge:
+    """The exchange blocks of a key-split decode merged by peer stores (one per rank, CUDA IPC).
+
+    Created collectively by every rank of `group` (the process group carries the handles once, at
+    set-up; the steps use none). Each rank allocates its block (attn_flash_peer_block_bytes,
+    zeroed), exports it, imports every peer's, and keeps the epoch counter the kernel's flags
+    use. `close()` (collective) unmaps the peers' blocks."""
+
+    def __init__(self, rows: int, D: int, group=None, device=None):
+        self.rank, self.world = _rank_world(group, None, None)
+        if self.world > ts.ATTN_PEERS_MAX:
+            raise ValueError(f"at most {ts.ATTN_PEERS_MAX} ranks")
+        self.group = group
+        self.rows, self.D = rows, D
+        nbytes = ts.attn_flash_peer_block_bytes(self.world, rows, D)
+        if nbytes == 0:
+            raise ValueError("bad exchange block shape")
+        self.block = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        torch.cuda.synchronize(self.block.device)
+        handle = ts.attn_peer_export(self.block) if self.world > 1 else b""
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, handle, group=group)
+        self.handles = handles
+        self.addrs = [self.block.data_ptr() if r == self.rank else ts.attn_peer_import(handles[r])
+                      for r in range(self.world)]
+        self.epoch = 0
+        if self.world > 1:
+            dist.barrier(group=group)  # every block mapped everywhere before the first store
+
+    def close(self):
+        if self.world > 1:
+            dist.barrier(group=self.group)  # nobody stores into a block being unmapped
+        for r, a in enumerate(self.addrs):
+            if r != self.rank and a:
+                ts.attn_peer_close(a, self.handles[r])
+        self.addrs = []
+
+
+def sharded_decode_peers(q, k_shard, v_shard, O, Hq: int, Hkv: int, Sq: int, Sk_total: int, k_begin: int, D: int,
+                         causal: int, scratch, merge: PeerMerge, bk: int = ts.ATTN_BK_DEFAULT, stream=None):
+    """sharded_decode with the merge done by one kernel over NVLink instead of the NCCL
+    all-gather and the combine: the partial kernel on this rank's key shard, then the peer
+    merge kernel, which leaves the full O [Hq*Sq*D] fp32 on every rank. Every rank makes every
+    call, in the same order. Raises AttnError on a library error."""
+    Sk_local = k_shard.numel() // (Hkv * D) if k_shard is not None else 0
+    merge.epoch += 1
+    rc = ts.attn_flash_decode_peers_stream(q, k_shard if Sk_local else None, v_shard if Sk_local else None, O, Hq,
+                                           Hkv, Sq, Sk_local, Sk_total, k_begin, D, causal, bk, scratch, merge.addrs,
+                                           merge.world, merge.rank, merge.epoch, stream)
+    if rc != ts.ATTN_OK:
+        raise ts.AttnError(rc, "attn_flash_decode_peers_stream")
     return O
