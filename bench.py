@@ -423,6 +423,35 @@ def run_ours(args, w) -> None:
     roof["peak_source"] = peaks["source"] + (" burst" if not decode else " copy")
     roof["kernel"] = "ts::fa_tc_kernel (tcgen05 + TMA + TMEM)"
 
+    def time_steps(fn, steps: int, what: str) -> float:
+        """ms per step of `fn(i)` over `steps` calls after 3 warm-up calls (CUDA events on the
+        launching stream, barrier and synchronize on both sides, max over ranks)."""
+        for i in range(3):
+            fn(i)
+        barrier()
+        e0.record(stream)
+        for i in range(steps):
+            fn(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t = max_over_ranks(e0.elapsed_time(e1)) / steps
+        rc, code = ts.attn_flash_status(scratch, stream)
+        if rc != ts.ATTN_OK:
+            raise ts.AttnError(rc, f"{what} device status {code}")
+        return t
+
+    def device_inputs(wl, seed: int, n: int):
+        """Seeded bf16 tensor of n elements with workload wl's distribution, made on the GPU."""
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        a, b = wl[8]
+        if wl[6] == "normal":
+            x = torch.randn(n, device=dev, generator=g) * b + a
+        else:
+            x = torch.rand(n, device=dev, generator=g) * (b - a) + a
+        return x.to(torch.bfloat16).view(torch.int16)
+
     # ---------------- the same prefill with causal masking (bottom-right), same buffers
     causal_line = None
     if not decode and not causal and not args.no_causal:
@@ -663,36 +692,18 @@ def run_ours(args, w) -> None:
                      "frac_of_measured_hbm_per_gpu": lby / (lms / 1e3) / 1e9 / world / peaks["hbm_gbs"],
                      "bytes_per_step": lby, "steps": lsteps, "scaling": "strong (key axis split over ranks)",
                      "merge": "one NCCL all-gather of packed (m, l, acc) fp32 blocks, then combine"}
+        # the same decode merged by the peer-store kernel (no collective per step)
+        merge = multigpu.PeerMerge(Hq5, lD, device=dev)
+        pms = time_steps(lambda i: multigpu.sharded_decode_peers(lq, lk, lv, lo, Hq5, Hkv5, 1, lSk, k0, lD, 0,
+                                                                 scratch, merge), lsteps, "long decode (peer merge)")
+        merge.close()
+        long_line["peer_merge"] = {
+            "value": lby / (pms / 1e3) / 1e9, "unit": "GB/s", "per_gpu_gbs": lby / (pms / 1e3) / 1e9 / world,
+            "ms_per_step": pms, "frac_of_measured_hbm_per_gpu": lby / (pms / 1e3) / 1e9 / world / peaks["hbm_gbs"],
+            "merge": "attn_flash_decode_peers_stream: the partial kernel, then one kernel that stores each rank's "
+                     "(m, l, acc) into every peer's exchange block over NVLink (CUDA IPC), raises flags, waits and "
+                     "merges -- no collective per step"}
         del lq, lk, lv, lo
-
-    def time_steps(fn, steps: int, what: str) -> float:
-        """ms per step of `fn(i)` over `steps` calls after 3 warm-up calls (CUDA events on the
-        launching stream, barrier and synchronize on both sides, max over ranks)."""
-        for i in range(3):
-            fn(i)
-        barrier()
-        e0.record(stream)
-        for i in range(steps):
-            fn(i)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier()
-        t = max_over_ranks(e0.elapsed_time(e1)) / steps
-        rc, code = ts.attn_flash_status(scratch, stream)
-        if rc != ts.ATTN_OK:
-            raise ts.AttnError(rc, f"{what} device status {code}")
-        return t
-
-    def device_inputs(wl, seed: int, n: int):
-        """Seeded bf16 tensor of n elements with workload wl's distribution, made on the GPU."""
-        g = torch.Generator(device=dev)
-        g.manual_seed(seed)
-        a, b = wl[8]
-        if wl[6] == "normal":
-            x = torch.randn(n, device=dev, generator=g) * b + a
-        else:
-            x = torch.rand(n, device=dev, generator=g) * (b - a) + a
-        return x.to(torch.bfloat16).view(torch.int16)
 
     # ---------------- the other BASELINE configs on each GPU (device-timed)
     config_lines = []
@@ -716,12 +727,12 @@ def run_ours(args, w) -> None:
 
             cms = time_steps(cfg_step, max(3, min(args.steps, 200)), name)
             if is_decode(cw):
-                work, unit, peak = algo_bytes(cHq, cHkv, cSq, cSk, cD) / 1e9, "GB/s", peaks["hbm_gbs"]
+                cwork, cunit, cpeak = algo_bytes(cHq, cHkv, cSq, cSk, cD) / 1e9, "GB/s", peaks["hbm_gbs"]
             else:
-                work, unit, peak = flops(cHq, cSq, cSk, cD, cc) / 1e12, "TFLOP/s", peaks["bf16_tflops"]
-            per = work / (cms / 1e3)
-            config_lines.append({"workload": name, "desc": cw[9], "value": world * per, "unit": unit,
-                                 "per_gpu": per, "ms_per_step": cms, "frac_of_measured_peak": per / peak,
+                cwork, cunit, cpeak = flops(cHq, cSq, cSk, cD, cc) / 1e12, "TFLOP/s", peaks["bf16_tflops"]
+            per = cwork / (cms / 1e3)
+            config_lines.append({"workload": name, "desc": cw[9], "value": world * per, "unit": cunit,
+                                 "per_gpu": per, "ms_per_step": cms, "frac_of_measured_peak": per / cpeak,
                                  "bound": "hbm" if is_decode(cw) else "tensor",
                                  "steps": max(3, min(args.steps, 200)),
                                  "l2": f"rotating pool of {cn} sets (>= 2x L2)", "data": "synthetic, seeded on device"})
