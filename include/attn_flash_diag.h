@@ -40,7 +40,9 @@ int attn_diag_exp2(const float *x, float *y, int n, int method, void *stream);
  * (Hq / Hkv) * Sq <= 128) in a build whose producer never loads Q, so the MMA issuer's bounded
  * wait for Q runs out after its limit (about 2 s) and every role of every CTA unwinds: the
  * kernel returns, O is left unwritten, and attn_flash_status(scratch, ...) reports
- * ATTN_ERR_DEVICE with ATTN_DEV_TIMEOUT_Q set in the device code. The context stays usable.
+ * ATTN_ERR_DEVICE with ATTN_DEV_TIMEOUT_Q in the device code -- or ATTN_DEV_TIMEOUT_KV: the
+ * producer's wait for a K/V slot the MMA never frees starts at the same moment, and whichever
+ * wait expires first is reported. The context stays usable.
  * scratch: at least attn_flash_scratch_bytes(128, bk) bytes. */
 int attn_diag_wait_timeout(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O, int Hq,
                            int Hkv, int Sq, int Sk, void *scratch, void *stream);

@@ -89,7 +89,7 @@ def _exp2_inputs() -> np.ndarray:
 def test_exp2_polynomial_accuracy(cuda_dev):
     """The FMA-pipe 2^x (round-to-nearest range reduction, degree-3 polynomial, exponent added
     to the bits): relative error <= 1.02e-4 over [-125, 0] (the fitted polynomial's own bound;
-    bf16 rounding of P, next, is 3.9e-3), exactly 2^n at every integer n, and no denormal or
+    bf16 rounding of P, next, is 2^-9 relative), exactly 2^n at every integer n, and no denormal or
     zero result anywhere in that range."""
     x = _exp2_inputs()
     x = x[(x >= -125.0) & (x <= 0.0)]
@@ -124,8 +124,10 @@ def test_exp2_mufu_accuracy(cuda_dev):
 def test_bounded_wait_runs_out_and_is_reported(cuda_dev):
     """The kernel build whose producer never loads Q: the MMA issuer's wait for Q runs out after
     its ~2 s limit, every role unwinds (in-flight K/V copies drained, TMEM freed), the call ends
-    with ATTN_DEV_TIMEOUT_Q in the status word, O is untouched, and the next ordinary call on the
-    same context is correct."""
+    with a timeout in the status word, O is untouched, and the next ordinary call on the same
+    context is correct. The producer's wait for a free K/V slot starts at the same moment and
+    runs out just as long after, so whichever of the two expires first is the one reported (the
+    other role sees the abort flag and returns without a report)."""
     Hq, Hkv, Sq, Sk, D = 8, 4, 32, 1024, 128
     Q, K, V = oracle.seeded_inputs(Hq, Hkv, Sq, Sk, D, seed=12)
     q, k, v = to_dev(Q, cuda_dev), to_dev(K, cuda_dev), to_dev(V, cuda_dev)
@@ -135,7 +137,8 @@ def test_bounded_wait_runs_out_and_is_reported(cuda_dev):
     assert ts.attn_diag_wait_timeout(q, k, v, o, Hq, Hkv, Sq, Sk, scratch) == ts.ATTN_OK
     rc, code = ts.attn_flash_status(scratch)
     dt = time.perf_counter() - t0
-    assert rc == ts.ATTN_ERR_DEVICE and code & ts.ATTN_DEV_TIMEOUT_Q, (rc, code)
+    assert rc == ts.ATTN_ERR_DEVICE and code & (ts.ATTN_DEV_TIMEOUT_Q | ts.ATTN_DEV_TIMEOUT_KV), (rc, code)
+    assert not code & (ts.ATTN_DEV_BAD_PAGE | ts.ATTN_DEV_BAD_POS | ts.ATTN_DEV_TIMEOUT_PEER), code
     assert 1.0 < dt < 30.0, dt  # the wait's ~2 s limit, not a hang
     assert torch.isnan(o).all()
     assert ts.attn_flash_status(scratch) == (ts.ATTN_OK, 0)  # read-and-clear

@@ -187,8 +187,15 @@ static int ts_run(fa_problem *p, void *scratch, void *stream) {
         p->part_l = p->out_l;
         p->part_acc = p->out_acc;
     }
-    int rc = ts_clear_status(s.status, stream);
-    if (rc != ATTN_OK) return rc;
+    /* the tensor-core kernel clears the status word itself (no memset between two launches,
+     * so consecutive calls can overlap under programmatic dependent launch); the general path
+     * needs the memset */
+    if (ts_tc_supported(p)) {
+        p->status_gen = ts_next_status_gen();
+    } else {
+        int rc = ts_clear_status(s.status, stream);
+        if (rc != ATTN_OK) return rc;
+    }
     return ts_launch_attention(p, stream);
 }
 

@@ -26,6 +26,16 @@ extern "C" unsigned long long attn_flash_kernel_launches(void) {
     return g_kernel_launches.load(std::memory_order_relaxed);
 }
 
+static std::atomic<unsigned> g_status_gen{0};
+
+extern "C" unsigned ts_next_status_gen(void) {
+    unsigned g;
+    do {
+        g = g_status_gen.fetch_add(1, std::memory_order_relaxed) + 1;
+    } while (g == 0);
+    return g;
+}
+
 namespace ts {
 
 __device__ __forceinline__ float ex2f(float x) {
@@ -136,6 +146,8 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const float *__restrict
                                                          size_t ps_ml, size_t ps_acc, float *__restrict__ out,
                                                          float *__restrict__ out_m, float *__restrict__ out_l,
                                                          int out_bf16) {
+    pdl_wait();  // the partials come from the previous grid of the stream
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (r >= rows) return;
@@ -201,6 +213,8 @@ template <int NP>
 __global__ void __launch_bounds__(256) fa_combine_few(const float *__restrict__ m, const float *__restrict__ l,
                                                       const float *__restrict__ acc, int rows, int D, size_t ps_ml,
                                                       size_t ps_acc, float *__restrict__ out, int out_bf16) {
+    pdl_wait();  // the partials come from the previous grid of the stream
+    pdl_trigger();
     const int cpr = D >> 2;  // float4 chunks per row (D % 4 == 0)
     const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     const long long r = idx / cpr;
@@ -265,6 +279,25 @@ extern "C" int ts_cc_major(void) {
     return cached_device_attr(cached, cudaDevAttrComputeCapabilityMajor, -1);
 }
 
+// Launches with programmatic dependent launch allowed: the grid may start while the previous
+// grid of the stream finishes; the kernel's pdl_wait() orders its memory accesses after it.
+template <typename... KArgs, typename... Args>
+static int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...) != cudaSuccess) return ATTN_ERR_CUDA;
+    ts_count_launch();
+    return ATTN_OK;
+}
+
 extern "C" int ts_launch_combine_strided(const float *m, const float *l, const float *acc, int nparts, int rows,
                                          int D, size_t ps_ml, size_t ps_acc, float *O, float *out_m, float *out_l,
                                          int out_bf16, void *stream) {
@@ -272,31 +305,21 @@ extern "C" int ts_launch_combine_strided(const float *m, const float *l, const f
     const int warps = 8;
     dim3 grid((rows + warps - 1) / warps);
     const bool vec = (D % 4 == 0) && (ps_acc % 4 == 0) && ((((uintptr_t)acc) | ((uintptr_t)O)) & 15u) == 0;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (vec && !out_m && nparts >= 2 && nparts <= 4) {
-        cudaStream_t st = static_cast<cudaStream_t>(stream);
         const long long threads = (long long)rows * (D / 4);
         const dim3 g((unsigned)((threads + 255) / 256));
-        if (nparts == 2)
-            ts::fa_combine_few<2><<<g, 256, 0, st>>>(m, l, acc, rows, D, ps_ml, ps_acc, O, out_bf16);
-        else if (nparts == 3)
-            ts::fa_combine_few<3><<<g, 256, 0, st>>>(m, l, acc, rows, D, ps_ml, ps_acc, O, out_bf16);
-        else
-            ts::fa_combine_few<4><<<g, 256, 0, st>>>(m, l, acc, rows, D, ps_ml, ps_acc, O, out_bf16);
-        if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
-        ts_count_launch();
-        return ATTN_OK;
+        if (nparts == 2) return launch_pdl(ts::fa_combine_few<2>, g, dim3(256), st, m, l, acc, rows, D, ps_ml, ps_acc,
+                                           O, out_bf16);
+        if (nparts == 3) return launch_pdl(ts::fa_combine_few<3>, g, dim3(256), st, m, l, acc, rows, D, ps_ml, ps_acc,
+                                           O, out_bf16);
+        return launch_pdl(ts::fa_combine_few<4>, g, dim3(256), st, m, l, acc, rows, D, ps_ml, ps_acc, O, out_bf16);
     }
     if (vec)
-        ts::fa_combine_kernel<true><<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows,
-                                                                                               D, ps_ml, ps_acc, O,
-                                                                                               out_m, out_l, out_bf16);
-    else
-        ts::fa_combine_kernel<false><<<grid, 32 * warps, 0, static_cast<cudaStream_t>(stream)>>>(m, l, acc, nparts, rows,
-                                                                                                D, ps_ml, ps_acc, O,
-                                                                                                out_m, out_l, out_bf16);
-    if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
-    ts_count_launch();
-    return ATTN_OK;
+        return launch_pdl(ts::fa_combine_kernel<true>, grid, dim3(32 * warps), st, m, l, acc, nparts, rows, D, ps_ml,
+                          ps_acc, O, out_m, out_l, out_bf16);
+    return launch_pdl(ts::fa_combine_kernel<false>, grid, dim3(32 * warps), st, m, l, acc, nparts, rows, D, ps_ml,
+                      ps_acc, O, out_m, out_l, out_bf16);
 }
 
 extern "C" int ts_launch_combine(const float *m, const float *l, const float *acc, int nparts, int rows, int D,

@@ -79,6 +79,9 @@ struct TcParams {
     const int *block_table, *seq_lens;
     int paged, page_size, max_pages, num_pages, hkv_local;
     float scale_log2;
+    // 0: the host cleared the status word before the launch; otherwise CTA 0 clears it and then
+    // publishes this call's generation in status[1] (error reports wait for that, report_error)
+    unsigned gen;
 };
 
 template <int DP, int NQT>
@@ -102,11 +105,11 @@ __device__ __forceinline__ uint32_t f2u(float f) { return __float_as_uint(f); }
 
 // Waits without honouring the abort flag: used only at teardown, to let TMA copies and MMAs
 // that are already in flight land before the CTA releases its shared memory and TMEM.
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int *status) {
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int *status, unsigned gen) {
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(bar, parity)) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            if (status) atomicOr(status, kDevErrTimeoutDrain);
+            report_error(status, kDevErrTimeoutDrain, gen);
             return;
         }
     }
@@ -248,6 +251,15 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // The set-up above touches no global memory, so it may overlap the previous grid of the
+    // stream (programmatic dependent launch); everything below comes after that grid.
+    pdl_wait();
+    pdl_trigger();
+    if (p.gen != 0 && blockIdx.x == 0 && threadIdx.x == 0) {
+        *reinterpret_cast<volatile int *>(p.status) = 0;
+        __threadfence();
+        atomicExch(reinterpret_cast<unsigned *>(p.status) + 1, p.gen);
+    }
 
     // Register budgets per warpgroup (NQT=2 launches 384 threads x 168 registers): the
     // producer/MMA warpgroup gives registers up, the two softmax warpgroups take them:
@@ -279,7 +291,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             const int used = (it.sk + P - 1) / P;  // pages that hold this sequence's keys
             const int *row = p.block_table + (size_t)b * p.max_pages;
             if (lane == 0) {
-                if (qi > 0 && !mbar_wait(q_empty, (qi - 1) & 1, abort_flag, p.status, kDevErrTimeoutQ)) ok = false;
+                if (qi > 0 && !mbar_wait(q_empty, (qi - 1) & 1, abort_flag, p.status, kDevErrTimeoutQ, p.gen)) ok = false;
                 if (ok) {
                     mbar_expect_tx(q_full, NQT * C::QTILE);
 #pragma unroll
@@ -315,7 +327,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                     if (bad) {
                         if (lane == 0) {
                             *abort_flag = 1;
-                            atomicOr(p.status, kDevErrBadPage);
+                            report_error(p.status, kDevErrBadPage, p.gen);
                         }
                         ok = false;
                         break;
@@ -326,7 +338,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 const uint32_t bar = kv_full(slot);
                 if (lane == 0) {
                     if (round > 0 &&
-                        !mbar_wait(kv_empty(slot), (round - 1) & 1, abort_flag, p.status, kDevErrTimeoutKV))
+                        !mbar_wait(kv_empty(slot), (round - 1) & 1, abort_flag, p.status, kDevErrTimeoutKV, p.gen))
                         ok = false;
                     else
                         mbar_expect_tx(bar, C::KVTILE);  // armed before any lane's copy can land
@@ -353,9 +365,9 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             }
         }
         if (!ok && lane == 0) {  // let the copies already in flight land before the CTA exits
-            if (q_inflight) drain_wait(q_full, qi & 1, p.status);
+            if (q_inflight) drain_wait(q_full, qi & 1, p.status, p.gen);
             for (uint32_t i = gl > (uint32_t)NS ? gl - NS : 0u; i < gl; ++i)
-                drain_wait(kv_full(i % NS), (i / NS) & 1, p.status);
+                drain_wait(kv_full(i % NS), (i / NS) & 1, p.status, p.gen);
         }
         __syncwarp();
     } else if (warp == 0) {
@@ -371,7 +383,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 if (it.nblk == 0) continue;
                 const int kv = it.kv, kb0 = it.kb0;
                 // the previous item's QKs have all finished reading Q
-                if (qi > 0 && !mbar_wait(q_empty, (qi - 1) & 1, abort_flag, p.status, kDevErrTimeoutQ)) {
+                if (qi > 0 && !mbar_wait(q_empty, (qi - 1) & 1, abort_flag, p.status, kDevErrTimeoutQ, p.gen)) {
                     ok = false;
                     break;
                 }
@@ -390,7 +402,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                     const int slot = gl % NS;
                     const int round = gl / NS;
                     if (round > 0 &&
-                        !mbar_wait(kv_empty(slot), (round - 1) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                        !mbar_wait(kv_empty(slot), (round - 1) & 1, abort_flag, p.status, kDevErrTimeoutKV, p.gen)) {
                         ok = false;
                         break;
                     }
@@ -418,9 +430,9 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 }
             }
             if (!ok) {  // let the copies already in flight land before the CTA exits
-                if (q_inflight) drain_wait(q_full, qi & 1, p.status);
+                if (q_inflight) drain_wait(q_full, qi & 1, p.status, p.gen);
                 for (uint32_t i = gl > (uint32_t)NS ? gl - NS : 0u; i < gl; ++i)
-                    drain_wait(kv_full(i % NS), (i / NS) & 1, p.status);
+                    drain_wait(kv_full(i % NS), (i / NS) & 1, p.status, p.gen);
             }
         }
     } else if (warp == 1) {
@@ -464,8 +476,8 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 const int nblk = it.nblk;
                 if (nblk == 0) continue;
                 const uint32_t sK0 = gc % NS;
-                ok = mbar_wait_fast(q_full, qi & 1, abort_flag, p.status, kDevErrTimeoutQ) &&
-                     mbar_wait_fast(kv_full(sK0), (gc / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV);
+                ok = mbar_wait_fast(q_full, qi & 1, abort_flag, p.status, kDevErrTimeoutQ, p.gen) &&
+                     mbar_wait_fast(kv_full(sK0), (gc / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV, p.gen);
                 if (!ok) break;
                 tc_fence_after();
 #pragma unroll
@@ -484,16 +496,16 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                         // V_j and K_{j+1} are normally resident long before P_t(j): waiting for
                         // them first keeps the P handoff the only wait between the softmax and
                         // the issue
-                        if (t == 0 && !mbar_wait_fast(kv_full(sV), (iV / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                        if (t == 0 && !mbar_wait_fast(kv_full(sV), (iV / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV, p.gen)) {
                             ok = false;
                             break;
                         }
                         if (t == 0 && more &&
-                            !mbar_wait_fast(kv_full(sK), (iK / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV)) {
+                            !mbar_wait_fast(kv_full(sK), (iK / NS) & 1, abort_flag, p.status, kDevErrTimeoutKV, p.gen)) {
                             ok = false;
                             break;
                         }
-                        if (!mbar_wait_fast(p_full(t), pp & 1, abort_flag, p.status, kDevErrTimeoutP)) {
+                        if (!mbar_wait_fast(p_full(t), pp & 1, abort_flag, p.status, kDevErrTimeoutP, p.gen)) {
                             ok = false;
                             break;
                         }
@@ -517,7 +529,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             }
             // Every MMA issued above must finish before TMEM is released.
             tc_commit(done_bar);
-            drain_wait(done_bar, 0, p.status);
+            drain_wait(done_bar, 0, p.status, p.gen);
         }
         __syncwarp();
     }
@@ -572,7 +584,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             // does the warp redo the block exactly below (rare: the first block sets a max that
             // later blocks seldom exceed by that much).
             const bool spec = full && __all_sync(0xffffffffu, m != -INFINITY);
-            ok = mbar_wait(s_full(t), sp & 1, abort_flag, p.status, kDevErrTimeoutS);
+            ok = mbar_wait(s_full(t), sp & 1, abort_flag, p.status, kDevErrTimeoutS, p.gen);
             ++sp;
             ok = __all_sync(0xffffffffu, ok);
             if (!ok) break;
@@ -729,7 +741,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
         }
         bool have_o = false;
         if (ok && nblk > 0) {
-            have_o = mbar_wait(o_full(t), op & 1, abort_flag, p.status, kDevErrTimeoutS);
+            have_o = mbar_wait(o_full(t), op & 1, abort_flag, p.status, kDevErrTimeoutS, p.gen);
             ++op;
             have_o = __all_sync(0xffffffffu, have_o);
             ok = have_o;
@@ -849,8 +861,18 @@ static int launch_tc_inst(cudaStream_t st, const CUtensorMap &tmQ, const CUtenso
             return ATTN_ERR_CUDA;
         if (cached) attr_done[dev].store(1, std::memory_order_release);
     }
-    kern<<<grid, C::THREADS, C::SMEM, st>>>(tmQ, tmK, tmV, prm);
-    if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
+    // programmatic dependent launch: the kernel's set-up may overlap the previous grid's tail
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(C::THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, tmQ, tmK, tmV, prm) != cudaSuccess) return ATTN_ERR_CUDA;
     ts_count_launch();
     return ATTN_OK;
 }
@@ -912,6 +934,7 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     prm.num_pages = P->num_pages;
     prm.hkv_local = P->hkv_local > 0 ? P->hkv_local : 1;
     prm.scale_log2 = P->scale_log2;
+    prm.gen = P->status_gen;
     prm.group = group;
     prm.head_units = (P->Sq % (kBM * NQT) == 0) ? P->Sq / (kBM * NQT) : 0;
     const int sms = ts_num_sms() > 0 ? ts_num_sms() : 1;

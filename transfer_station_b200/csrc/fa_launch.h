@@ -47,6 +47,10 @@ typedef struct fa_problem {
     const int *block_table, *seq_lens;
     int paged, page_size, max_pages, num_pages, hkv_local;
     float scale_log2;          /* (1/sqrt(D)) * log2(e) */
+    /* 0: the caller cleared the status word before the launch. Otherwise the tensor-core
+     * kernel clears it itself (CTA 0 zeroes status[0], then stores this value in status[1];
+     * error reports wait for that store), so no memset has to sit between two launches. */
+    unsigned status_gen;
 } fa_problem;
 
 /* Number of SMs of the current device (cached). */
@@ -103,6 +107,9 @@ typedef struct ts_rope_problem {
 
 int ts_launch_qkv_rope(const ts_rope_problem *p, void *stream);
 int ts_launch_rope_table(float *cos_sin, int max_pos, int rot, double theta, void *stream);
+
+/* A fresh nonzero status generation (fa_problem.status_gen), unique within the process. */
+unsigned ts_next_status_gen(void);
 
 /* Zero the device status word (async). */
 int ts_clear_status(int *status, void *stream);

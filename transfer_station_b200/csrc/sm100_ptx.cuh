@@ -70,10 +70,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Programmatic dependent launch. pdl_wait: returns once the grids this one depends on in its
+// stream have completed and their memory is visible (at once when the launch did not allow an
+// early start); every thread calls it before its first global-memory access. pdl_trigger: lets
+// the next grid of the stream that allows it start launching while this one still runs.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ORs `code` into the status word status[0]. gen == 0: the host cleared the word before the
+// launch. gen != 0: the kernel clears it itself -- CTA 0 zeroes status[0], then publishes gen in
+// status[1] -- so a report first waits (bounded) until that clear is visible, and the clear can
+// never erase it.
+__device__ __forceinline__ void report_error(int *status, int code, unsigned gen) {
+    if (!status) return;
+    if (gen != 0) {
+        const uint64_t t0 = globaltimer_ns();
+        while (ld_acquire_gpu(reinterpret_cast<const unsigned *>(status) + 1) != gen &&
+               globaltimer_ns() - t0 < kWaitLimitNs) {
+        }
+    }
+    atomicOr(status, code);
+}
+
 // Bounded wait for the phase with the given parity to complete. Returns false (and leaves
 // the abort flag set) when the CTA is aborting or the limit ran out.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                          int *status, int code) {
+                                          int *status, int code, unsigned gen = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
@@ -81,7 +109,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         if (*abort_flag) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
             *abort_flag = 1;
-            if (status) atomicOr(status, code);
+            report_error(status, code, gen);
             return false;
         }
     }
@@ -91,7 +119,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
 // the abort flag and the clock are read on every 64th poll only, so a phase that completes
 // while the waiter is in that bookkeeping is seen sooner.
 __device__ __forceinline__ bool mbar_wait_fast(uint32_t bar, uint32_t parity, volatile int *abort_flag,
-                                               int *status, int code) {
+                                               int *status, int code, unsigned gen = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t i = 1;; ++i) {
@@ -100,7 +128,7 @@ __device__ __forceinline__ bool mbar_wait_fast(uint32_t bar, uint32_t parity, vo
             if (*abort_flag) return false;
             if (globaltimer_ns() - t0 > kWaitLimitNs) {
                 *abort_flag = 1;
-                if (status) atomicOr(status, code);
+                report_error(status, code, gen);
                 return false;
             }
         }
@@ -349,9 +377,9 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 // reduction x = n + f, f in [-1/2, 1/2], done with the 1.5*2^23 shift (t = x + 1.5*2^23 holds
 // n in its low mantissa bits); 2^f by a degree-3 polynomial with constant term exactly 1 and
 // coefficients fitted (numpy, iteratively reweighted least squares toward minimax relative
-// error) over [-1/2, 1/2], max relative error 1.0e-4 -- 20x below the bf16 rounding that P
-// gets next; 2^n applied by adding n to the exponent field (bits(t) << 23 == n << 23 mod
-// 2^32). Inputs are clamped at -125 so the result stays a normal float (2^-125 ~ 2e-38 where
+// error) over [-1/2, 1/2], max relative error 1.02e-4 (reached at f = -1/2) -- 19x below the
+// bf16 rounding (2^-9 relative) that P gets next; 2^n applied by adding n to the exponent field
+// (bits(t) << 23 == n << 23 mod 2^32). Inputs are clamped at -125 so the result stays a normal float (2^-125 ~ 2e-38 where
 // the exact value is smaller: irrelevant next to a denominator >= 1).
 __device__ __forceinline__ float2 exp2_fma2(float2 x) {
     constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
