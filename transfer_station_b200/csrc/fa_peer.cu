@@ -70,13 +70,49 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
     return v;
 }
 
-// One warp per row at a time; lane i owns columns i, i+32, ... (any D <= 256).
+// Merges `n` partials of one row, for the 32 columns [col0, col0 + 32) of that row (one per
+// lane): m_at(s), l_at(s) and acc_at(s, col) give part s's m, l and acc element. The lanes load the parts'
+// m and l in parallel (one round trip for up to 32 parts), and the acc loads of all parts are
+// independent, so they are in flight together. Returns the merged (m, L) and the lane's
+// unnormalised acc column.
+template <typename M, typename L, typename A>
+__device__ __forceinline__ float3 merge_parts(int n, int lane, int col, int D, M m_at, L l_at, A acc_at) {
+    float mx = -INFINITY;
+    for (int s = lane; s < n; s += 32) mx = fmaxf(mx, m_at(s));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float Lsum = 0.f, a = 0.f;
+    for (int s0 = 0; s0 < n; s0 += 32) {
+        const int s = s0 + lane;
+        float w = 0.f;
+        if (s < n) {
+            const float ms = m_at(s);
+            w = (ms != -INFINITY) ? ex2_approx(ms - mx) : 0.f;
+            Lsum = fmaf(w, l_at(s), Lsum);
+        }
+        const int cnt = min(32, n - s0);
+#pragma unroll 8
+        for (int k = 0; k < cnt; ++k) {
+            const float wk = __shfl_sync(0xffffffffu, w, k);
+            if (col < D) a = fmaf(wk, acc_at(s0 + k, col), a);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
+    return make_float3(mx, Lsum, a);
+}
+
+// The CTA's (row, 32-column chunk) tasks are spread over its warps; lane i owns column
+// chunk * 32 + i (any D <= 256).
 __global__ void __launch_bounds__(256) fa_peer_merge_kernel(const PeerParams p) {
-    constexpr int kMaxU = ATTN_D_MAX / 32;
     __shared__ int s_fail;
+    pdl_wait();  // the key pieces come from the previous grid of the stream
+    pdl_trigger();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int c = blockIdx.x;
     const int r0 = c * p.rows_per_cta, r1 = min(p.rows, r0 + p.rows_per_cta);
+    const int nchunk = (p.D + 31) / 32;
+    const int ntask = max(0, r1 - r0) * nchunk;
     const int buf = (int)(p.epoch & 1u);
     const size_t slot_bytes = peer_slot_bytes(p.rows, p.D);
     const size_t ml = (2 * (size_t)p.rows + 3) & ~(size_t)3;
@@ -85,46 +121,28 @@ __global__ void __launch_bounds__(256) fa_peer_merge_kernel(const PeerParams p) 
     };
     if (threadIdx.x == 0) s_fail = 0;
 
-    // 1. merge this rank's key pieces and store the result into every rank's slot `rank`
-    for (int r = r0 + warp; r < r1; r += nwarps) {
-        float mx = -INFINITY;
-        for (int s = lane; s < p.nparts; s += 32) mx = fmaxf(mx, p.m[(size_t)s * p.rows + r]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float L = 0.f;
-        for (int s = lane; s < p.nparts; s += 32) {
-            const float ms = p.m[(size_t)s * p.rows + r];
-            if (ms != -INFINITY) L = fmaf(ex2_approx(ms - mx), p.l[(size_t)s * p.rows + r], L);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        float a[kMaxU];
-#pragma unroll
-        for (int u = 0; u < kMaxU; ++u) a[u] = 0.f;
-        for (int s = 0; s < p.nparts; ++s) {
-            const float ms = p.m[(size_t)s * p.rows + r];
-            const float w = (ms != -INFINITY) ? ex2_approx(ms - mx) : 0.f;
-            const float *src = p.acc + ((size_t)s * p.rows + r) * p.D;
-#pragma unroll
-            for (int u = 0; u < kMaxU; ++u) {
-                const int col = lane + 32 * u;
-                if (col < p.D) a[u] = fmaf(w, src[col], a[u]);
-            }
+    // 1. merge this rank's key pieces; one rank: that is the output. Otherwise store the merged
+    //    (m, l, acc) into slot `rank` of every rank's block.
+    for (int t = warp; t < ntask; t += nwarps) {
+        const int r = r0 + t / nchunk, col = (t % nchunk) * 32 + lane;
+        const float3 v = merge_parts(
+            p.nparts, lane, col, p.D, [&](int s) { return p.m[(size_t)s * p.rows + r]; },
+            [&](int s) { return p.l[(size_t)s * p.rows + r]; },
+            [&](int s, int cc) { return p.acc[((size_t)s * p.rows + r) * p.D + cc]; });
+        if (p.world == 1) {
+            if (col < p.D) p.O[(size_t)r * p.D + col] = v.y > 0.f ? v.z / v.y : 0.f;
+            continue;
         }
         for (int q = 0; q < p.world; ++q) {
             float *dst = slot(p.blocks[q], p.rank);
-            if (lane == 0) {
-                dst[r] = mx;
-                dst[p.rows + r] = L;
+            if (lane == 0 && col == 0) {
+                dst[r] = v.x;
+                dst[p.rows + r] = v.y;
             }
-            float *dacc = dst + ml + (size_t)r * p.D;
-#pragma unroll
-            for (int u = 0; u < kMaxU; ++u) {
-                const int col = lane + 32 * u;
-                if (col < p.D) dacc[col] = a[u];
-            }
+            if (col < p.D) dst[ml + (size_t)r * p.D + col] = v.z;
         }
     }
+    if (p.world == 1) return;
 
     // 2. this CTA's rows are in every block: raise its flag everywhere (system-scope release)
     __threadfence_system();
@@ -156,39 +174,13 @@ __global__ void __launch_bounds__(256) fa_peer_merge_kernel(const PeerParams p) 
 
     // 4. merge the world slots of this CTA's rows into O (L2-coherent reads of peer-written data)
     unsigned char *own = p.blocks[p.rank];
-    for (int r = r0 + warp; r < r1; r += nwarps) {
-        float mx = -INFINITY;
-        for (int s = lane; s < p.world; s += 32) mx = fmaxf(mx, __ldcg(slot(own, s) + r));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float L = 0.f;
-        for (int s = lane; s < p.world; s += 32) {
-            const float *sl = slot(own, s);
-            const float ms = __ldcg(sl + r);
-            if (ms != -INFINITY) L = fmaf(ex2_approx(ms - mx), __ldcg(sl + p.rows + r), L);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-        const float inv = (L > 0.f) ? 1.f / L : 0.f;
-        float a[kMaxU];
-#pragma unroll
-        for (int u = 0; u < kMaxU; ++u) a[u] = 0.f;
-        for (int s = 0; s < p.world; ++s) {
-            const float *sl = slot(own, s);
-            const float ms = __ldcg(sl + r);
-            const float w = (ms != -INFINITY) ? ex2_approx(ms - mx) : 0.f;
-            const float *src = sl + ml + (size_t)r * p.D;
-#pragma unroll
-            for (int u = 0; u < kMaxU; ++u) {
-                const int col = lane + 32 * u;
-                if (col < p.D) a[u] = fmaf(w, __ldcg(src + col), a[u]);
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < kMaxU; ++u) {
-            const int col = lane + 32 * u;
-            if (col < p.D) p.O[(size_t)r * p.D + col] = a[u] * inv;
-        }
+    for (int t = warp; t < ntask; t += nwarps) {
+        const int r = r0 + t / nchunk, col = (t % nchunk) * 32 + lane;
+        const float3 v = merge_parts(
+            p.world, lane, col, p.D, [&](int s) { return __ldcg(slot(own, s) + r); },
+            [&](int s) { return __ldcg(slot(own, s) + p.rows + r); },
+            [&](int s, int cc) { return __ldcg(slot(own, s) + ml + (size_t)r * p.D + cc); });
+        if (col < p.D) p.O[(size_t)r * p.D + col] = v.y > 0.f ? v.z / v.y : 0.f;
     }
 }
 
@@ -220,8 +212,17 @@ extern "C" int ts_launch_peer_merge(const float *m, const float *l, const float 
     // same rows, so each CTA waits for the same CTA index of its peers
     const int ctas = rows < ts::kPeerMaxCtas ? (rows > 0 ? rows : 1) : ts::kPeerMaxCtas;
     p.rows_per_cta = (rows + ctas - 1) / ctas;
-    ts::fa_peer_merge_kernel<<<ctas, 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
-    if (cudaGetLastError() != cudaSuccess) return ATTN_ERR_CUDA;
+    // programmatic dependent launch: may start while the partial kernel finishes (pdl_wait)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ctas);
+    cfg.blockDim = dim3(256);
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, ts::fa_peer_merge_kernel, p) != cudaSuccess) return ATTN_ERR_CUDA;
     ts_count_launch();
     return ATTN_OK;
 }
