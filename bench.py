@@ -794,6 +794,9 @@ def run_ours(args, w) -> None:
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": int(Q.nbytes + K.nbytes + V.nbytes),
                     "d2h_bytes_per_step": int(Hq * Sq * D * 4), "steps": e2e_steps,
+                    "pcie_gbs": (Q.nbytes + K.nbytes + V.nbytes + Hq * Sq * D * 4) * e2e_steps / (e2e_ms / 1e3) / 1e9,
+                    "bound": "PCIe: the host<->device bytes of a step (pcie_gbs, both directions overlapped) take "
+                             "longer than its kernel",
                     "path": "pinned host -> cudaMemcpyAsync -> attn_flash_stream -> cudaMemcpyAsync -> pinned host",
                     "pipeline": "2 CUDA streams on alternate steps (double-buffered device, host and scratch "
                                 "buffers): a step's readback overlaps the next step's upload"},

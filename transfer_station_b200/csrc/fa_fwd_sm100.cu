@@ -53,6 +53,7 @@ namespace ts {
 constexpr int kBM = 128;              // query rows per tile (TMEM lanes)
 constexpr int kBN = ATTN_GPU_KEY_TILE;  // keys per tile
 constexpr float kRescaleLog2 = 8.0f;  // lazy max update threshold, in log2 units
+constexpr float kRedoSum = 256.0f;    // 2^kRescaleLog2: a speculative row sum above it means a redo
 constexpr int kSmemBudget = 200 * 1024;
 
 struct TcParams {
@@ -578,11 +579,14 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             // cut). The choice must be warp-uniform: every path issues warp-collective tcgen05.st.
             const bool full = __all_sync(0xffffffffu, nv >= kBN);
             // `spec`: a full block of a warp whose rows all have a running max. P is computed
-            // against that max while the block's own max is tracked alongside, so the
-            // exponentials do not wait for a max pass over all 128 columns first. Only when some
-            // row's block max exceeds its running max by more than kRescaleLog2 (in log2 units)
-            // does the warp redo the block exactly below (rare: the first block sets a max that
-            // later blocks seldom exceed by that much).
+            // against that max, so the exponentials do not wait for a max pass over all 128
+            // columns first. A row whose block max exceeds its running max by more than
+            // kRescaleLog2 (in log2 units) has a P above 2^kRescaleLog2, so its row sum is above
+            // it too; only then (any row of the warp) is the block redone exactly below. Every P is
+            // positive, so a row sum within the bound proves each of its P is -- no per-element max
+            // is tracked. The redo is rare: the first block sets a max that later blocks seldom
+            // exceed by that much (a sum above the bound with no single P above it only costs
+            // the exact pass).
             const bool spec = full && __all_sync(0xffffffffu, m != -INFINITY);
             ok = mbar_wait(s_full(t), sp & 1, abort_flag, p.status, kDevErrTimeoutS, p.gen);
             ++sp;
@@ -595,11 +599,13 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             if (spec) {
                 const float2 nms2 = make_float2(-ms, -ms);
                 float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-                float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
                 // 16 score columns at a time: each load (and its wait) is issued right before
                 // the previous chunk's P store, and the chunk boundaries keep the compiler's
                 // schedule chunk by chunk (one upfront 128-column load measured 13% slower).
-                // 2 of every 8 pairs take the polynomial exp2 on the FMA pipe, the rest MUFU.
+                // Exponentials: all on MUFU with two tiles per CTA (prefill: the MUFU unit has
+                // room, and the polynomial's FMA-pipe instructions cost issue slots); with one
+                // tile (decode, where MUFU is the bottleneck) 2 of every 8 pairs take the
+                // polynomial exp2 on the FMA pipe.
                 tmem_ld16p(tS, sr);
 #pragma unroll
                 for (int cc = 0; cc < 8; ++cc) {
@@ -607,10 +613,9 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
                         const float s0 = u2f(sr[16 * cc + 2 * u]), s1 = u2f(sr[16 * cc + 2 * u + 1]);
-                        mx[u & 3] = fmax3(mx[u & 3], s0, s1);
                         const float2 x = __ffma2_rn(make_float2(s0, s1), c2, nms2);
                         float2 pr;
-                        if (u < 2) {
+                        if (NQT == 1 && u < 2) {
                             pr = exp2_fma2(x);
                         } else {
                             pr.x = ex2(x.x);
@@ -628,8 +633,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 }
                 rs0 = acc0.x + acc1.x;
                 rs1 = acc0.y + acc1.y;
-                const float mb = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-                redo = __any_sync(0xffffffffu, mb > m && (mb - m) * sl2 > kRescaleLog2);
+                redo = __any_sync(0xffffffffu, rs0 + rs1 > kRedoSum);
                 if (redo) tmem_wait_st();  // the speculative P stores land before the exact ones
             } else if (__all_sync(0xffffffffu, nv <= 0)) {
                 // No row of this warp sees any key of the block (a causal tile below the
