@@ -599,9 +599,10 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             if (spec) {
                 const float2 nms2 = make_float2(-ms, -ms);
                 float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-                // 16 score columns at a time: each load (and its wait) is issued right before
-                // the previous chunk's P store, and the chunk boundaries keep the compiler's
-                // schedule chunk by chunk (one upfront 128-column load measured 13% slower).
+                // 16 score columns at a time: the next chunk's load is issued before this
+                // chunk's exponentials and waited for after its P store, and the chunk boundaries
+                // keep the compiler's schedule chunk by chunk (one upfront 128-column load
+                // measured 13% slower).
                 // Exponentials: all on MUFU with two tiles per CTA (prefill: the MUFU unit has
                 // room, and the polynomial's FMA-pipe instructions cost issue slots); with one
                 // tile (decode, where MUFU is the bottleneck) 2 of every 8 pairs take the
@@ -610,6 +611,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
 #pragma unroll
                 for (int cc = 0; cc < 8; ++cc) {
                     uint32_t pk[8];
+                    if (cc < 7) tmem_ld16_nowait(tS + 16 * (cc + 1), sr + 16 * (cc + 1));
 #pragma unroll
                     for (int u = 0; u < 8; ++u) {
                         const float s0 = u2f(sr[16 * cc + 2 * u]), s1 = u2f(sr[16 * cc + 2 * u + 1]);
@@ -627,9 +629,8 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                             acc0 = __fadd2_rn(acc0, pr);
                         pk[u] = pack_bf16x2(pr.x, pr.y);
                     }
-                    // P of chunk cc goes to columns [8cc, 8cc+8), scores that were already read
-                    if (cc < 7) tmem_ld16p(tS + 16 * (cc + 1), sr + 16 * (cc + 1));
                     tmem_st8(tS + cc * 8, pk);
+                    if (cc < 7) tmem_wait_ld16(sr + 16 * (cc + 1));
                 }
                 rs0 = acc0.x + acc1.x;
                 rs1 = acc0.y + acc1.y;

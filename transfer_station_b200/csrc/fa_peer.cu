@@ -64,24 +64,28 @@ __device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+__device__ __forceinline__ unsigned ld_relaxed_sys(const unsigned *p) {
     unsigned v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
-// Merges `n` partials of one row, for the 32 columns [col0, col0 + 32) of that row (one per
-// lane): m_at(s), l_at(s) and acc_at(s, col) give part s's m, l and acc element. The lanes load the parts'
-// m and l in parallel (one round trip for up to 32 parts), and the acc loads of all parts are
-// independent, so they are in flight together. Returns the merged (m, L) and the lane's
-// unnormalised acc column.
-template <typename M, typename L, typename A>
-__device__ __forceinline__ float3 merge_parts(int n, int lane, int col, int D, M m_at, L l_at, A acc_at) {
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// Merges `n` partials of one row for the VW consecutive columns [col, col + VW) a lane owns:
+// m_at(s) and l_at(s) give part s's m and l, acc_at(s, col, out) loads its VW acc values. The
+// lanes load the parts' m and l in parallel (one round trip for up to 32 parts), and the acc loads
+// of all parts are independent, so they are in flight together. Returns the merged m and L; `a`
+// receives the lane's unnormalised acc values.
+template <int VW, typename M, typename L, typename A>
+__device__ __forceinline__ float2 merge_parts(int n, int lane, bool live, M m_at, L l_at, A acc_at, float (&a)[VW]) {
     float mx = -INFINITY;
     for (int s = lane; s < n; s += 32) mx = fmaxf(mx, m_at(s));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float Lsum = 0.f, a = 0.f;
+    float Lsum = 0.f;
+#pragma unroll
+    for (int e = 0; e < VW; ++e) a[e] = 0.f;
     for (int s0 = 0; s0 < n; s0 += 32) {
         const int s = s0 + lane;
         float w = 0.f;
@@ -91,19 +95,46 @@ __device__ __forceinline__ float3 merge_parts(int n, int lane, int col, int D, M
             Lsum = fmaf(w, l_at(s), Lsum);
         }
         const int cnt = min(32, n - s0);
-#pragma unroll 8
+#pragma unroll 4
         for (int k = 0; k < cnt; ++k) {
             const float wk = __shfl_sync(0xffffffffu, w, k);
-            if (col < D) a = fmaf(wk, acc_at(s0 + k, col), a);
+            if (live) {
+                float x[VW];
+                acc_at(s0 + k, x);
+#pragma unroll
+                for (int e = 0; e < VW; ++e) a[e] = fmaf(wk, x[e], a[e]);
+            }
         }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, o);
-    return make_float3(mx, Lsum, a);
+    return make_float2(mx, Lsum);
 }
 
-// The CTA's (row, 32-column chunk) tasks are spread over its warps; lane i owns column
-// chunk * 32 + i (any D <= 256).
+template <int VW>
+__device__ __forceinline__ void load_vec(const float *src, float (&x)[VW], bool coherent) {
+    if constexpr (VW == 4) {
+        const float4 v = coherent ? __ldcg(reinterpret_cast<const float4 *>(src)) : *reinterpret_cast<const float4 *>(src);
+        x[0] = v.x;
+        x[1] = v.y;
+        x[2] = v.z;
+        x[3] = v.w;
+    } else {
+        x[0] = coherent ? __ldcg(src) : *src;
+    }
+}
+
+template <int VW>
+__device__ __forceinline__ void store_vec(float *dst, const float (&x)[VW]) {
+    if constexpr (VW == 4)
+        *reinterpret_cast<float4 *>(dst) = make_float4(x[0], x[1], x[2], x[3]);
+    else
+        *dst = x[0];
+}
+
+// The CTA's (row, 32*VW-column chunk) tasks are spread over its warps; lane i owns the VW
+// columns chunk * 32 * VW + VW * i (VW = 4 when D % 4 == 0: 16-byte loads and NVLink stores).
+template <int VW>
 __global__ void __launch_bounds__(256) fa_peer_merge_kernel(const PeerParams p) {
     __shared__ int s_fail;
     pdl_wait();  // the key pieces come from the previous grid of the stream
@@ -111,7 +142,8 @@ __global__ void __launch_bounds__(256) fa_peer_merge_kernel(const PeerParams p) 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int c = blockIdx.x;
     const int r0 = c * p.rows_per_cta, r1 = min(p.rows, r0 + p.rows_per_cta);
-    const int nchunk = (p.D + 31) / 32;
+    constexpr int CW = 32 * VW;  // columns per task
+    const int nchunk = (p.D + CW - 1) / CW;
     const int ntask = max(0, r1 - r0) * nchunk;
     const int buf = (int)(p.epoch & 1u);
     const size_t slot_bytes = peer_slot_bytes(p.rows, p.D);
@@ -124,13 +156,20 @@ __global__ void __launch_bounds__(256) fa_peer_merge_kernel(const PeerParams p) 
     // 1. merge this rank's key pieces; one rank: that is the output. Otherwise store the merged
     //    (m, l, acc) into slot `rank` of every rank's block.
     for (int t = warp; t < ntask; t += nwarps) {
-        const int r = r0 + t / nchunk, col = (t % nchunk) * 32 + lane;
-        const float3 v = merge_parts(
-            p.nparts, lane, col, p.D, [&](int s) { return p.m[(size_t)s * p.rows + r]; },
+        const int r = r0 + t / nchunk, col = (t % nchunk) * CW + VW * lane;
+        const bool live = col < p.D;
+        float a[VW];
+        const float2 v = merge_parts<VW>(
+            p.nparts, lane, live, [&](int s) { return p.m[(size_t)s * p.rows + r]; },
             [&](int s) { return p.l[(size_t)s * p.rows + r]; },
-            [&](int s, int cc) { return p.acc[((size_t)s * p.rows + r) * p.D + cc]; });
+            [&](int s, float(&x)[VW]) { load_vec<VW>(p.acc + ((size_t)s * p.rows + r) * p.D + col, x, false); }, a);
         if (p.world == 1) {
-            if (col < p.D) p.O[(size_t)r * p.D + col] = v.y > 0.f ? v.z / v.y : 0.f;
+            if (live) {
+                const float inv = v.y > 0.f ? 1.f / v.y : 0.f;
+#pragma unroll
+                for (int e = 0; e < VW; ++e) a[e] *= inv;
+                store_vec<VW>(p.O + (size_t)r * p.D + col, a);
+            }
             continue;
         }
         for (int q = 0; q < p.world; ++q) {
@@ -139,48 +178,56 @@ __global__ void __launch_bounds__(256) fa_peer_merge_kernel(const PeerParams p) 
                 dst[r] = v.x;
                 dst[p.rows + r] = v.y;
             }
-            if (col < p.D) dst[ml + (size_t)r * p.D + col] = v.z;
+            if (live) store_vec<VW>(dst + ml + (size_t)r * p.D + col, a);
         }
     }
     if (p.world == 1) return;
 
-    // 2. this CTA's rows are in every block: raise its flag everywhere (system-scope release)
-    __threadfence_system();
+    // 2. this CTA's rows are in every block: raise its flag everywhere. The CTA barrier orders
+    //    every thread's stores before thread 0's one system-scope release (fences are cumulative
+    //    over what the fencing thread has synchronised with), which orders them before the flags.
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence_system();
         for (int q = 0; q < p.world; ++q) {
             unsigned *flags = reinterpret_cast<unsigned *>(p.blocks[q]);
             st_release_sys(flags + (size_t)p.rank * kPeerMaxCtas + c, p.epoch);
         }
     }
 
-    // 3. wait (bounded) for every rank's flag of this CTA in the own block
+    // 3. wait (bounded) for every rank's flag of this CTA in the own block: relaxed polls, then
+    //    one acquire fence once the flag is seen; the CTA barrier passes it on to every thread
     if (threadIdx.x < p.world) {
         const unsigned *flag =
             reinterpret_cast<const unsigned *>(p.blocks[p.rank]) + (size_t)threadIdx.x * kPeerMaxCtas + c;
         const uint64_t t0 = globaltimer_ns();
-        while ((int)(ld_acquire_sys(flag) - p.epoch) < 0) {
+        while ((int)(ld_relaxed_sys(flag) - p.epoch) < 0) {
             if (globaltimer_ns() - t0 > kWaitLimitNs) {
                 atomicOr(p.status, kDevErrTimeoutPeer);
                 s_fail = 1;
                 break;
             }
         }
+        fence_acq_rel_sys();
     }
     __syncthreads();
     if (s_fail) return;
-    __threadfence_system();
 
     // 4. merge the world slots of this CTA's rows into O (L2-coherent reads of peer-written data)
     unsigned char *own = p.blocks[p.rank];
     for (int t = warp; t < ntask; t += nwarps) {
-        const int r = r0 + t / nchunk, col = (t % nchunk) * 32 + lane;
-        const float3 v = merge_parts(
-            p.world, lane, col, p.D, [&](int s) { return __ldcg(slot(own, s) + r); },
+        const int r = r0 + t / nchunk, col = (t % nchunk) * CW + VW * lane;
+        const bool live = col < p.D;
+        float a[VW];
+        const float2 v = merge_parts<VW>(
+            p.world, lane, live, [&](int s) { return __ldcg(slot(own, s) + r); },
             [&](int s) { return __ldcg(slot(own, s) + p.rows + r); },
-            [&](int s, int cc) { return __ldcg(slot(own, s) + ml + (size_t)r * p.D + cc); });
-        if (col < p.D) p.O[(size_t)r * p.D + col] = v.y > 0.f ? v.z / v.y : 0.f;
+            [&](int s, float(&x)[VW]) { load_vec<VW>(slot(own, s) + ml + (size_t)r * p.D + col, x, true); }, a);
+        if (live) {
+            const float inv = v.y > 0.f ? 1.f / v.y : 0.f;
+#pragma unroll
+            for (int e = 0; e < VW; ++e) a[e] *= inv;
+            store_vec<VW>(p.O + (size_t)r * p.D + col, a);
+        }
     }
 }
 
@@ -222,7 +269,10 @@ extern "C" int ts_launch_peer_merge(const float *m, const float *l, const float 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, ts::fa_peer_merge_kernel, p) != cudaSuccess) return ATTN_ERR_CUDA;
+    const bool vec = D % 4 == 0 && ((((uintptr_t)acc) | ((uintptr_t)O)) & 15u) == 0;
+    const cudaError_t e = vec ? cudaLaunchKernelEx(&cfg, ts::fa_peer_merge_kernel<4>, p)
+                              : cudaLaunchKernelEx(&cfg, ts::fa_peer_merge_kernel<1>, p);
+    if (e != cudaSuccess) return ATTN_ERR_CUDA;
     ts_count_launch();
     return ATTN_OK;
 }
