@@ -484,16 +484,17 @@ def run_ours(args, w) -> None:
                        "flops": "useful (query i sees keys <= Sk - Sq + i)", "steps": csteps}
 
     # ---------------- e2e through the C ABI with pinned host buffers
-    # Two CUDA streams take alternate steps, each with its own device buffers, pinned output
-    # buffer and scratch block: step i's readback (device -> host) runs while step i+1's inputs
-    # go up (host -> device) -- PCIe moves both directions at once -- and the kernels run in
-    # between. Every step still copies its Q, K, V up and its O back inside the timed region.
+    # E2E_LANES CUDA streams take turns, each with its own device buffers, pinned output buffer
+    # and scratch block: step i's readback (device -> host) runs while step i+1's inputs go up
+    # (host -> device) -- PCIe moves both directions at once -- and the kernels run in between.
+    # Every step still copies its Q, K, V up and its O back inside the timed region.
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     hq = torch.from_numpy(Q.view(np.int16)).pin_memory()
     hk = torch.from_numpy(K.view(np.int16)).pin_memory()
     hv = torch.from_numpy(V.view(np.int16)).pin_memory()
     lanes = []
-    for ln in range(2):
+    n_lanes = max(1, args.e2e_lanes)
+    for ln in range(n_lanes):
         if ln < ncopy:
             dq, dk, dv, do = qs[ln], ks[ln], vs[ln], os_[ln]
         else:
@@ -505,7 +506,7 @@ def run_ours(args, w) -> None:
         lanes.append((dq, dk, dv, do, st, scr, ho))
 
     def e2e_step(i: int):
-        dq, dk, dv, do, st, scr, ho = lanes[i & 1]
+        dq, dk, dv, do, st, scr, ho = lanes[i % n_lanes]
         with torch.cuda.stream(st):
             dq.copy_(hq, non_blocking=True)
             dk.copy_(hk, non_blocking=True)
@@ -515,14 +516,16 @@ def run_ours(args, w) -> None:
                 raise ts.AttnError(rc, "attn_flash_stream (e2e)")
             ho.copy_(do, non_blocking=True)
 
-    for i in range(2):
+    for i in range(n_lanes):
         e2e_step(i)
     barrier()
     e0.record(stream)
-    lanes[1][4].wait_stream(stream)
+    for ln in lanes[1:]:
+        ln[4].wait_stream(stream)
     for i in range(e2e_steps):
         e2e_step(i)
-    stream.wait_stream(lanes[1][4])
+    for ln in lanes[1:]:
+        stream.wait_stream(ln[4])
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -798,7 +801,7 @@ def run_ours(args, w) -> None:
                     "bound": "PCIe: the host<->device bytes of a step (pcie_gbs, both directions overlapped) take "
                              "longer than its kernel",
                     "path": "pinned host -> cudaMemcpyAsync -> attn_flash_stream -> cudaMemcpyAsync -> pinned host",
-                    "pipeline": "2 CUDA streams on alternate steps (double-buffered device, host and scratch "
+                    "pipeline": f"{n_lanes} CUDA streams taking turns (their own device, host and scratch "
                                 "buffers): a step's readback overlaps the next step's upload"},
             "gpu_launches": int(launches),
             "clocks": csum,
@@ -827,6 +830,7 @@ def main():
                     help="sequences of 16384 tokens in the producer line (4 = the config 5 prefill shape)")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--e2e-steps", type=int, default=200)
+    ap.add_argument("--e2e-lanes", type=int, default=3, help="CUDA streams taking turns in the e2e line")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
