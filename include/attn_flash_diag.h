@@ -27,6 +27,13 @@ extern "C" {
 #define ATTN_DEV_BAD_POS 64       /* a token position outside the rotary table or the cache */
 #define ATTN_DEV_TIMEOUT_PEER 128 /* a peer GPU's partials never arrived (multi-GPU merge) */
 
+/* The work plan attn_flash_stream would use for this problem on the tensor-core path of a GPU
+ * with `sms` SMs: pure host arithmetic, no device is touched. out[0..4] = nsplit (key pieces
+ * per unit), keys_per_split, n_direct (units run whole before a split last wave, 0 when every
+ * unit is split or none is), row_base (first query row of the split units), units (query-row
+ * tiles x kv heads). Returns ATTN_OK or ATTN_ERR_ARGS. */
+int attn_diag_plan(int Hq, int Hkv, int Sq, int Sk, int D, int causal, int sms, int out[5]);
+
 /* Writes the 32-bit pattern `bits` into every lane and column of the tensor memory (TMEM) of
  * every SM, by CTAs that allocate all 512 columns, store, and free them again. */
 int attn_diag_fill_tmem(uint32_t bits, void *stream);

@@ -12,6 +12,7 @@ from __future__ import annotations
 import ctypes
 import os
 from pathlib import Path
+from typing import NamedTuple
 
 PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "lib" / "libattn_flash_b200.so"
@@ -87,6 +88,7 @@ EXPORTS = {
     # include/attn_flash_diag.h
     "attn_diag_fill_tmem": (ctypes.c_int, [ctypes.c_uint32, ctypes.c_void_p]),
     "attn_diag_exp2": (ctypes.c_int, [_f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "attn_diag_plan": (ctypes.c_int, [ctypes.c_int] * 7 + [ctypes.POINTER(ctypes.c_int)]),
     "attn_diag_wait_timeout": (ctypes.c_int, [_u16p, _u16p, _u16p, _f32p] + [ctypes.c_int] * 4 +
                                [ctypes.c_void_p, ctypes.c_void_p]),
     # include/attn_qkv_rope.h
@@ -306,6 +308,24 @@ def attn_diag_fill_tmem(bits: int, stream=None) -> int:
 def attn_diag_exp2(x, y, n, method, stream=None) -> int:
     """Diagnostic: y = 2^x by the attention kernel's polynomial (method 0) or MUFU (method 1)."""
     return int(load_library().attn_diag_exp2(_ptr(x), _ptr(y), n, method, _stream_handle(stream)))
+
+
+class Plan(NamedTuple):
+    """The work plan of attn_flash_stream for one problem (attn_diag_plan)."""
+    nsplit: int          # key pieces per split unit
+    keys_per_split: int
+    n_direct: int        # units run whole before a split last wave
+    row_base: int        # first query row of the split units
+    units: int           # query-row tiles x kv heads
+
+
+def attn_diag_plan(Hq, Hkv, Sq, Sk, D, causal, sms) -> Plan:
+    """Diagnostic: the tensor-core work plan for a GPU with `sms` SMs (host arithmetic only)."""
+    out = (ctypes.c_int * 5)()
+    rc = int(load_library().attn_diag_plan(Hq, Hkv, Sq, Sk, D, int(causal), sms, out))
+    if rc != ATTN_OK:
+        raise AttnError(rc, "attn_diag_plan")
+    return Plan(*[int(v) for v in out])
 
 
 def attn_diag_wait_timeout(Q, K, V, O, Hq, Hkv, Sq, Sk, scratch, stream=None) -> int:

@@ -12,6 +12,7 @@
 #include <string.h>
 
 #include "attn_flash.h"
+#include "attn_flash_diag.h"
 #include "fa_launch.h"
 
 /* flash.c:641-647: a bk the caller did not also size scratch with must fail loudly, never
@@ -96,12 +97,10 @@ const char *attn_flash_strerror(int status) {
  * tensor-core path without causal masking, the tail wave: when the last wave of CTAs would
  * run at most half full, its L units are split into floor(SMs / L) key pieces, so the last
  * wave takes a fraction of a full CTA's time; their partials are merged afterwards. */
-static void ts_plan(fa_problem *p) {
-    const int tc = ts_tc_supported(p);
+static void ts_plan_core(fa_problem *p, int tc, int sms, int ctas) {
     const long long rows = (long long)p->Hq * p->Sq;
     const int nblk = (p->Sk + ATTN_GPU_KEY_TILE - 1) / ATTN_GPU_KEY_TILE;
-    const int sms = ts_num_sms() > 0 ? ts_num_sms() : 1;
-    const int ctas = tc ? ts_tc_ctas_per_split(p) : (int)((rows + 7) / 8);
+    if (sms < 1) sms = 1;
     p->n_direct = 0;
     p->row_base = 0;
     long long cap = rows > 0 ? (long long)ATTN_PARTIAL_ROWS / rows : 0;
@@ -127,7 +126,7 @@ static void ts_plan(fa_problem *p) {
     if (best > 1 || !tc || p->causal || ctas <= sms) return;
     const int L = ctas % sms;
     if (L == 0 || 2 * L > sms) return;
-    const int ur = ts_tc_unit_rows(p);
+    const int ur = ts_tc_unit_rows(p); /* query rows per unit */
     const int tiles = ctas / p->Hkv;
     const int u0 = ctas - L;
     const long long rows_per_kv = (long long)(p->Hq / p->Hkv) * p->Sq;
@@ -141,6 +140,12 @@ static void ts_plan(fa_problem *p) {
     p->keys_per_split = bps * ATTN_GPU_KEY_TILE;
     p->n_direct = u0;
     p->row_base = (int)row_base;
+}
+
+static void ts_plan(fa_problem *p) {
+    const int tc = ts_tc_supported(p);
+    const long long rows = (long long)p->Hq * p->Sq;
+    ts_plan_core(p, tc, ts_num_sms(), tc ? ts_tc_ctas_per_split(p) : (int)((rows + 7) / 8));
 }
 
 static int ts_validate(const void *Q, const void *K, const void *V, int Hq, int Hkv, int Sq, int Sk, int D,
@@ -171,6 +176,22 @@ static void ts_fill(fa_problem *p, const uint16_t *Q, const uint16_t *K, const u
     p->scale_log2 = (1.0f / sqrtf((float)D)) * 1.4426950408889634f;
     p->nsplit = 1;
     p->keys_per_split = ((Sk + ATTN_GPU_KEY_TILE - 1) / ATTN_GPU_KEY_TILE) * ATTN_GPU_KEY_TILE;
+}
+
+int attn_diag_plan(int Hq, int Hkv, int Sq, int Sk, int D, int causal, int sms, int out[5]) {
+    if (!out || Hq < 1 || Hkv < 1 || Hq % Hkv != 0 || Sq < 1 || Sk < 1 || D < 1 || D > ATTN_D_MAX || sms < 1)
+        return ATTN_ERR_ARGS;
+    if ((long long)Hq * Sq > 0x7fffffffLL || (long long)Hkv * Sk > 0x7fffffffLL) return ATTN_ERR_ARGS;
+    fa_problem p;
+    ts_fill(&p, NULL, NULL, NULL, Hq, Hkv, Sq, Sk, D, causal, 0);
+    const int ctas = ts_tc_ctas_per_split(&p);
+    ts_plan_core(&p, 1, sms, ctas);
+    out[0] = p.nsplit;
+    out[1] = p.keys_per_split;
+    out[2] = p.n_direct;
+    out[3] = p.row_base;
+    out[4] = ctas;
+    return ATTN_OK;
 }
 
 static int ts_run(fa_problem *p, void *scratch, void *stream) {

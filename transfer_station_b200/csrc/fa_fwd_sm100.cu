@@ -38,6 +38,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include <atomic>
 #include <type_traits>
@@ -70,6 +71,7 @@ struct TcParams {
     int row_base, part_rows;  // split units cover global rows [row_base, row_base + part_rows)
     int write_partials;
     int o_bf16;   // 1: O is bf16 bits (round to nearest even), else fp32
+    int o_tma;    // 1: fp32 O is written through the staging boxes by TMA (tmO maps O)
     int n_items;  // work items (units, or units and key pieces); the grid has min(n_items, SMs) CTAs
     int snake;    // 1: alternate the direction of the per-CTA item walk every round (causal)
     int group;    // query heads per kv head
@@ -92,8 +94,14 @@ struct TcConfig {
     static constexpr int NS_RAW = (kSmemBudget - NQT * QTILE) / KVTILE;
     static constexpr int NS = NS_RAW > 8 ? 8 : NS_RAW;  // K/V ring slots
     static constexpr int NBAR = 3 + 2 * NS + 3 * NQT;   // q_full/empty, done, kv_full/empty, s/p/o_full
-    static constexpr int PID_WIN = 512;  // paged K/V: page ids staged in shared memory at a time
-    static constexpr int SMEM = 1024 + NQT * QTILE + NS * KVTILE + NBAR * 8 + 16 + PID_WIN * 4;
+    static constexpr int PID_WIN = 256;  // paged K/V: page ids staged in shared memory at a time
+    // Output staging (two-tile instances): one [32 rows][32 fp32] box (128-byte rows, 128-byte
+    // swizzle) per softmax warp, written from registers and stored to O by TMA.
+    static constexpr int OSTAGE = 32 * 32 * 4;
+    static constexpr int NOSTAGE = NQT == 2 ? 8 : 0;  // one-tile instances keep per-row stores
+    static constexpr int SMEM = 1024 + NQT * QTILE + NS * KVTILE + NOSTAGE * OSTAGE + NBAR * 8 + 16;
+    static constexpr int smem_bytes(bool paged) { return SMEM + (paged ? PID_WIN * 4 : 0); }
+    static_assert(smem_bytes(true) <= 227 * 1024, "shared memory per CTA");
     static constexpr int THREADS = 128 + 128 * NQT;
     static constexpr uint32_t TMEM_COLS = (NQT * kBN + NQT * DP) <= 256 ? 256u : 512u;
     static_assert(NS >= 2, "K/V ring needs at least two slots");
@@ -129,7 +137,8 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int *s
 template <int DP, int NQT, bool VT, bool GENERAL, bool PAGED, bool NOQ = false>
 __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                 const __grid_constant__ CUtensorMap tmV, const TcParams p) {
+                 const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmO,
+                 const TcParams p) {
     using C = TcConfig<DP, NQT>;
     constexpr int NS = C::NS;
     constexpr int NBOX_D = DP / 64;     // 64-element (128-byte) boxes across the head dim
@@ -142,7 +151,8 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
 
     const uint32_t sQ = base_u32;
     const uint32_t sKV = base_u32 + NQT * C::QTILE;
-    const uint32_t bar0 = sKV + NS * C::KVTILE;
+    const uint32_t sO = sKV + NS * C::KVTILE;  // output staging, 1024-byte aligned
+    const uint32_t bar0 = sO + C::NOSTAGE * C::OSTAGE;
     const uint32_t q_full = bar0;         // Q tiles of an item landed
     const uint32_t q_empty = bar0 + 8;    // every QK of an item finished: Q may be reloaded
     const uint32_t done_bar = bar0 + 16;
@@ -243,6 +253,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
         tma_prefetch_desc(&tmQ);
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
+        if (p.o_tma) tma_prefetch_desc(&tmO);
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -758,7 +769,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
             const size_t grow = (size_t)kv * p.rows_per_kv + prow;  // row of [Hq*Sq]
             float *dst;
             float mult;
-            bool out_bf16 = false;
+            bool out_bf16 = false, to_o = false;
             if (GENERAL && (piece >= 0 || p.write_partials)) {
                 // (m, l, unnormalised acc): a key piece's slot, or the caller's partial row
                 const size_t slot = piece >= 0 ? (size_t)piece * p.part_rows + (grow - p.row_base) : grow;
@@ -774,6 +785,7 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                 dst = p.O + grow * D;  // bf16 output: element offsets of a uint16_t array
                 mult = (l > 0.f) ? 1.f / l : 0.f;
                 out_bf16 = p.o_bf16 != 0;
+                to_o = true;
             }
             auto store_rows = [&](auto bf16_tag) {
                 constexpr bool kBf16 = decltype(bf16_tag)::value;
@@ -806,13 +818,49 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
                     }
                 }
             };
-            if (out_bf16)
+            if (NQT == 2 && to_o && !out_bf16 && p.o_tma) {
+                // Normalised fp32 O through TMA: per 32-column chunk, each lane writes its row's
+                // 128 bytes into the warp's [32 rows][32 floats] box (16-byte piece v of row r
+                // at piece v ^ (r & 7), the 128-byte swizzle, so the eight lanes of a shared-
+                // memory phase hit distinct banks), then lane 0 stores the box to rows
+                // [y0, y0 + 32) of this kv head's output. Rows past rows_per_kv and columns past
+                // D lie outside the tensor map and are not written. (A per-row st.global.v4
+                // touches 32 cache lines per warp instruction.)
+                const uint32_t buf = sO + (uint32_t)(warp - 4) * C::OSTAGE;
+                const int y0 = row0 + t * kBM + quad * 32;
+#pragma unroll
+                for (int cc = 0; cc < DP / 32; ++cc) {
+                    if (cc * 32 >= D) break;
+                    uint32_t o[32];
+                    if (have_o) {
+                        tmem_ld32(tO + cc * 32, o);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 32; ++u) o[u] = 0u;
+                    }
+                    if (lane == 0) bulk_wait_read0();  // the previous box has been read out
+                    __syncwarp();
+#pragma unroll
+                    for (int v = 0; v < 8; ++v)
+                        st_shared_v4(buf + lane * 128 + ((v ^ (lane & 7)) << 4), u2f(o[4 * v]) * mult,
+                                     u2f(o[4 * v + 1]) * mult, u2f(o[4 * v + 2]) * mult, u2f(o[4 * v + 3]) * mult);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0 && y0 < p.rows_per_kv) {  // a box wholly past the rows is not stored
+                        tma_store_3d(&tmO, buf, cc * 32, y0, kv);
+                        bulk_commit();
+                    }
+                }
+            } else if (out_bf16) {
                 store_rows(std::true_type{});
-            else
+            } else {
                 store_rows(std::false_type{});
+            }
         }
         }
-        // teardown (softmax warpgroups): TMEM reads done before the dealloc below
+        // teardown (softmax warpgroups): this warp's output stores complete, TMEM reads done
+        // before the dealloc below
+        if (lane == 0) bulk_wait0();
         tc_fence_before();
         __syncthreads();
     }
@@ -836,6 +884,20 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
+// The fp32 output as a 3-D tensor map {D, rows_per_kv, Hkv} (the layout of Q) for the epilogue's
+// TMA stores: boxes of [32 rows][32 floats], 128-byte swizzle.
+static bool make_map_o(CUtensorMap *m, float *O, uint64_t D, uint64_t rows, uint64_t hkv) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {D, rows, hkv};
+    cuuint64_t strides[2] = {D * 4, rows * D * 4};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, O, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 // 3-D bf16 tensor map with 128-byte swizzle: dims {d0 (contiguous), d1, d2}, byte strides of
 // d1 and d2, box {64, box1, 1}. Out-of-range elements read as zero.
 static bool make_map_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
@@ -854,7 +916,7 @@ static bool make_map_3d(CUtensorMap *m, const void *base, uint64_t d0, uint64_t 
 
 template <int DP, int NQT, bool VT, bool GENERAL, bool PAGED, bool NOQ = false>
 static int launch_tc_inst(cudaStream_t st, const CUtensorMap &tmQ, const CUtensorMap &tmK, const CUtensorMap &tmV,
-                          const TcParams &prm, dim3 grid) {
+                          const CUtensorMap &tmO, const TcParams &prm, dim3 grid) {
     using C = TcConfig<DP, NQT>;
     auto kern = fa_tc_kernel<DP, NQT, VT, GENERAL, PAGED, NOQ>;
     static std::atomic<int> attr_done[64];  // the shared-memory opt-in, once per device
@@ -862,7 +924,8 @@ static int launch_tc_inst(cudaStream_t st, const CUtensorMap &tmQ, const CUtenso
     if (cudaGetDevice(&dev) != cudaSuccess) return ATTN_ERR_CUDA;
     const bool cached = dev >= 0 && dev < 64;
     if (!cached || !attr_done[dev].load(std::memory_order_acquire)) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::smem_bytes(PAGED)) !=
+            cudaSuccess)
             return ATTN_ERR_CUDA;
         if (cached) attr_done[dev].store(1, std::memory_order_release);
     }
@@ -870,14 +933,14 @@ static int launch_tc_inst(cudaStream_t st, const CUtensorMap &tmQ, const CUtenso
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(C::THREADS);
-    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.dynamicSmemBytes = C::smem_bytes(PAGED);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern, tmQ, tmK, tmV, prm) != cudaSuccess) return ATTN_ERR_CUDA;
+    if (cudaLaunchKernelEx(&cfg, kern, tmQ, tmK, tmV, tmO, prm) != cudaSuccess) return ATTN_ERR_CUDA;
     ts_count_launch();
     return ATTN_OK;
 }
@@ -904,8 +967,15 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
             return ATTN_ERR_CUDA;
         }
     }
+    CUtensorMap tmO;
+    memset(&tmO, 0, sizeof tmO);
+    // fp32 normalised output of a two-tile instance: stored by TMA (any other output keeps per-row
+    // stores)
+    const int o_tma = NQT == 2 && P->O != nullptr && !P->o_bf16 && !P->write_partials;
+    if (o_tma && !make_map_o(&tmO, P->O, D, rows, (uint64_t)P->Hkv)) return ATTN_ERR_CUDA;
     TcParams prm;
     prm.O = P->O;
+    prm.o_tma = o_tma;
     prm.out_m = P->out_m;
     prm.out_l = P->out_l;
     prm.out_acc = P->out_acc;
@@ -946,18 +1016,18 @@ static int launch_tc(const fa_problem *P, cudaStream_t st, int tiles_per_kv) {
     if constexpr (NOQ) {  // the diagnostic build: plain work plan only
         prm.n_items = units;
         prm.snake = 0;
-        return launch_tc_inst<DP, NQT, VT, false, false, true>(st, tmQ, tmK, tmV, prm, dim3(min(units, sms)));
+        return launch_tc_inst<DP, NQT, VT, false, false, true>(st, tmQ, tmK, tmV, tmO, prm, dim3(min(units, sms)));
     }
     if (prm.n_direct == units && !prm.write_partials && !P->paged) {
         prm.n_items = units;
         prm.snake = prm.causal;
-        return launch_tc_inst<DP, NQT, VT, false, false>(st, tmQ, tmK, tmV, prm, dim3(min(units, sms)));
+        return launch_tc_inst<DP, NQT, VT, false, false>(st, tmQ, tmK, tmV, tmO, prm, dim3(min(units, sms)));
     }
     prm.n_items = prm.n_direct + (units - prm.n_direct) * prm.pieces;
     prm.snake = 0;
     if (P->paged)  // paged K/V: the general work plan, V row-major
-        return launch_tc_inst<DP, NQT, false, true, true>(st, tmQ, tmK, tmV, prm, dim3(min(prm.n_items, sms)));
-    return launch_tc_inst<DP, NQT, VT, true, false>(st, tmQ, tmK, tmV, prm, dim3(min(prm.n_items, sms)));
+        return launch_tc_inst<DP, NQT, false, true, true>(st, tmQ, tmK, tmV, tmO, prm, dim3(min(prm.n_items, sms)));
+    return launch_tc_inst<DP, NQT, VT, true, false>(st, tmQ, tmK, tmV, tmO, prm, dim3(min(prm.n_items, sms)));
 }
 
 static int nqt_for(const fa_problem *P) {
