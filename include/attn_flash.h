@@ -226,9 +226,10 @@ int attn_flash_decode_peers_stream(const uint16_t *Q, const uint16_t *K, const u
  * declared by the library (held on every GPU that loads it until exit) and calls no
  * allocator. Accepts at most 4096 query rows (Hq*Sq) -- decode-shaped calls -- and returns
  * ATTN_ERR_ARGS beyond that. All calls on a device share the block: calls whose GPU work
- * overlaps race. The first call on a device looks the block up (make it before any stream
- * capture); the address is kept until exit, so do not call it on a device again after
- * cudaDeviceReset. Blocks until the work on `stream` is done; returns ATTN_OK or a status
+ * overlaps race. The first call on a device looks the block up; the address is kept until
+ * exit, so do not call it on a device again after cudaDeviceReset. Blocks until the work on
+ * `stream` is done (it synchronises the stream), so it is never captured into a CUDA graph: on
+ * a capturing stream it returns ATTN_ERR_ARGS and does nothing. Returns ATTN_OK or a status
  * code. */
 int attn_flash_noalloc(const uint16_t *Q, const uint16_t *K, const uint16_t *V, float *O, int Hq,
                        int Hkv, int Sq, int Sk, int D, int causal, int bk, int v_prepacked,

@@ -73,3 +73,23 @@ def test_noalloc_rejects_oversized_calls(cuda_dev):
     o = torch.zeros(Hq * Sq * D, dtype=torch.float32, device=cuda_dev)
     assert ts.attn_flash_noalloc(q, k, k, o, Hq, Hkv, Sq, Sk, D, 0, 128) == ts.ATTN_ERR_ARGS
     assert ts.attn_flash_noalloc(q, k, k, o, 8, 8, 1, 1 << 28, D, 0, 128) == ts.ATTN_ERR_ARGS
+
+
+def test_noalloc_refuses_a_capturing_stream(cuda_dev):
+    """Every call synchronises its stream, which a stream capture forbids: on a capturing stream
+    the call returns ATTN_ERR_ARGS before touching anything, and the capture stays usable."""
+    Hq, Hkv, Sq, Sk, D = 8, 2, 1, 256, 64
+    q = torch.zeros(Hq * Sq * D, dtype=torch.int16, device=cuda_dev)
+    k = torch.zeros(Hkv * Sk * D, dtype=torch.int16, device=cuda_dev)
+    o = torch.zeros(Hq * Sq * D, dtype=torch.float32, device=cuda_dev)
+    assert ts.attn_flash_noalloc(q, k, k, o, Hq, Hkv, Sq, Sk, D, 0, 128) == ts.ATTN_OK
+    s = torch.cuda.Stream(device=cuda_dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        rc = ts.attn_flash_noalloc(q, k, k, o, Hq, Hkv, Sq, Sk, D, 0, 128, stream=s)
+        o.add_(1.0)  # the capture still records work after the refused call
+    assert rc == ts.ATTN_ERR_ARGS
+    o.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.all(o == 1.0)

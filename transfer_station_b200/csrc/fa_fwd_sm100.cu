@@ -254,6 +254,26 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
         if (p.o_tma) tma_prefetch_desc(&tmO);
+        if constexpr (!PAGED && !NOQ) {
+            // The first item's Q tiles and K/V tile 0 into L2 while the previous grid finishes: the
+            // CTA's first loads, after the dependency wait below, then come from L2.
+            const int q0 = item_index(0);
+            if (q0 < p.n_items) {
+                const Item it = item_at(q0);
+                if (it.nblk > 0) {
+#pragma unroll
+                    for (int b = 0; b < NBOX_D; ++b) {
+#pragma unroll
+                        for (int t = 0; t < NQT; ++t) tma_prefetch_l2_3d(&tmQ, b * 64, it.row0 + t * kBM, it.kv);
+                        tma_prefetch_l2_3d(&tmK, b * 64, it.kb0, it.kv);
+                        if (!VT) tma_prefetch_l2_3d(&tmV, b * 64, it.kb0, it.kv);
+                    }
+                    if (VT)
+#pragma unroll
+                        for (int b = 0; b < kBN / 64; ++b) tma_prefetch_l2_3d(&tmV, it.kb0 + b * 64, 0, it.kv);
+                }
+            }
+        }
     }
     if (warp == 1) {
         tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -263,8 +283,9 @@ __global__ void __launch_bounds__(TcConfig<DP, NQT>::THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    // The set-up above touches no global memory, so it may overlap the previous grid of the
-    // stream (programmatic dependent launch); everything below comes after that grid.
+    // The set-up above reads no global memory (the L2 prefetch returns nothing to the thread), so
+    // it may overlap the previous grid of the stream (programmatic dependent launch); everything
+    // below comes after that grid.
     pdl_wait();
     pdl_trigger();
     if (p.gen != 0 && blockIdx.x == 0 && threadIdx.x == 0) {

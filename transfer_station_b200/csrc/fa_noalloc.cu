@@ -19,8 +19,9 @@
 //     is written earlier in the same call. Two calls whose GPU work overlaps (different
 //     streams, or different host threads) race on the block: serialise them.
 //   * The first call on a device looks up the block's device address with
-//     cudaGetSymbolAddress (under a mutex), with that device current. Make that first
-//     call before any stream capture begins. The address is kept for the life of the
+//     cudaGetSymbolAddress (under a mutex), with that device current. No call may be made
+//     while its stream is being captured (every call synchronises the stream): such a call
+//     returns ATTN_ERR_ARGS and touches nothing. The address is kept for the life of the
 //     process: after cudaDeviceReset on a device the library's module is loaded anew and the
 //     block may move, so a process that resets a device must not call this entry point on
 //     that device again.
@@ -94,6 +95,11 @@ extern "C" int attn_flash_noalloc(const uint16_t *Q, const uint16_t *K, const ui
         return ATTN_ERR_ARGS;
     }
     if (ts_cc_major() != 10) return ATTN_ERR_NOT_SM100;
+    // it synchronises the stream (the status readback), which no stream capture allows
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &cap) != cudaSuccess ||
+        cap != cudaStreamCaptureStatusNone)
+        return ATTN_ERR_ARGS;
     void *block = nullptr;
     int rc = noalloc_block(&block);
     if (rc != ATTN_OK) return rc;

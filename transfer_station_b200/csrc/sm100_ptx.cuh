@@ -149,6 +149,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *tm,
         : "memory");
 }
 
+// Asks L2 to fetch a box of the tensor (no data comes back to the issuing thread, so it observes
+// nothing and may be issued before the memory it covers is final: a later load still reads
+// whatever L2 holds then).
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap *tm, int c0, int c1, int c2) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(tm)),
+                 "r"(c0), "r"(c1), "r"(c2)
+                 : "memory");
+}
+
 // Tiled store of a shared-memory box to global memory (the async proxy reads the box; elements
 // outside the tensor map's extents are not written). Coordinates are never negative here.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap *tm, uint32_t src, int c0, int c1, int c2) {
