@@ -16,8 +16,8 @@ Keys of the JSON line beyond the base contract:
   cpu_baseline  the reference's own flash.c (oracle/_ref, compiled natively through the SVE
                 shim) timed on this host's cores on a bounded sample of the same workload
   e2e           the same metric through the C ABI with pinned host buffers: every step copies
-                Q, K, V host->device and O device->host inside the timed region; two CUDA
-                streams take alternate steps, so one step's readback overlaps the next upload
+                Q, K, V host->device and O device->host inside the timed region; three CUDA
+                streams take turns (--e2e-lanes), so one step's readback overlaps the next upload
   causal_prefill  the headline prefill with causal masking on the same buffers (useful FLOPs)
   decode        a secondary HBM-bound line: BASELINE config 3 (GQA decode, B=64, Sk=8192), per GPU
   paged_decode  the same decode through attn_flash_paged_stream (64-key pages, shuffled table)
