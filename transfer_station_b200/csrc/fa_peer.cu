@@ -184,14 +184,13 @@ __global__ void __launch_bounds__(256) fa_peer_merge_kernel(const PeerParams p) 
     if (p.world == 1) return;
 
     // 2. this CTA's rows are in every block: raise its flag everywhere. The CTA barrier orders
-    //    every thread's stores before thread 0's one system-scope release (fences are cumulative
-    //    over what the fencing thread has synchronised with), which orders them before the flags.
+    //    every thread's stores before the flag threads' system-scope releases (fences are
+    //    cumulative over what the fencing thread has synchronised with), which order them before
+    //    the flags; thread q releases to rank q, so the releases run side by side.
     __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int q = 0; q < p.world; ++q) {
-            unsigned *flags = reinterpret_cast<unsigned *>(p.blocks[q]);
-            st_release_sys(flags + (size_t)p.rank * kPeerMaxCtas + c, p.epoch);
-        }
+    if (threadIdx.x < p.world) {
+        unsigned *flags = reinterpret_cast<unsigned *>(p.blocks[threadIdx.x]);
+        st_release_sys(flags + (size_t)p.rank * kPeerMaxCtas + c, p.epoch);
     }
 
     // 3. wait (bounded) for every rank's flag of this CTA in the own block: relaxed polls, then
