@@ -315,8 +315,6 @@ int attn_flash_decode_peers_stream(const uint16_t *Q, const uint16_t *K, const u
     if ((long long)Hq * Sq > ATTN_PARTIAL_ROWS) return ATTN_ERR_ARGS;
     ts_scratch s;
     ts_scratch_layout(scratch, D, &s);
-    rc = ts_clear_status(s.status, stream);
-    if (rc != ATTN_OK) return rc;
     int nparts = 0;
     if (Sk_local > 0) {
         fa_problem p;
@@ -324,6 +322,14 @@ int attn_flash_decode_peers_stream(const uint16_t *Q, const uint16_t *K, const u
         p.Sk_total = Sk_total;
         p.k_begin = k_begin;
         p.status = s.status;
+        /* the tensor-core kernel clears the status word itself (no memset between this step's
+         * kernels and the previous step's, which keeps their launches overlapping) */
+        if (ts_tc_supported(&p)) {
+            p.status_gen = ts_next_status_gen();
+        } else {
+            rc = ts_clear_status(s.status, stream);
+            if (rc != ATTN_OK) return rc;
+        }
         ts_plan(&p);
         if (p.n_direct > 0) { /* a prefill tail split: run every unit whole instead */
             p.nsplit = 1;
@@ -339,6 +345,9 @@ int attn_flash_decode_peers_stream(const uint16_t *Q, const uint16_t *K, const u
         rc = ts_launch_attention_pieces(&p, stream);
         if (rc != ATTN_OK) return rc;
         nparts = p.nsplit;
+    } else {
+        rc = ts_clear_status(s.status, stream);
+        if (rc != ATTN_OK) return rc;
     }
     return ts_launch_peer_merge(s.m, s.l, s.acc, nparts, Hq * Sq, D, O, blocks, world, rank, epoch, s.status, stream);
 }
