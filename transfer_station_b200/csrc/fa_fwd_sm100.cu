@@ -11,8 +11,9 @@
 // Work decomposition. The `group` query heads that share kv head `kv` are contiguous in Q
 // ([Hq][Sq][D] == [Hkv][group*Sq][D]), so each kv head owns one packed [group*Sq][D]
 // matrix of query rows that all read the same K/V. A CTA takes NQT tiles of 128 packed
-// rows (256 rows for NQT=2) and streams the kv head's K/V tiles once for all of them.
-// grid = (row tiles per kv head, Hkv, key splits).
+// rows (256 rows for NQT=2) and streams the kv head's K/V tiles once for all of them. Such a
+// unit, or one key piece of it, is a work item; the grid has at most one CTA per SM, each
+// walking its share of the items (below).
 //
 // Roles (one CTA per SM): warp 0 issues TMA loads (Q once, then K_j, V_j alternating
 // through an NS-slot ring); warp 1 owns TMEM and issues the MMAs from one thread;
